@@ -1,0 +1,51 @@
+// Python bindings of the primus_dlrm_b200 core kernels (module `_C`).
+#include <torch/extension.h>
+
+namespace pd {
+// embedding.cu
+void emb_gather(std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, std::vector<at::Tensor>,
+                std::vector<at::Tensor>, at::Tensor, int64_t, at::Tensor);
+void emb_pooled(std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, std::vector<at::Tensor>,
+                std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, int64_t, at::Tensor);
+at::Tensor emb_keys(std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, std::vector<at::Tensor>,
+                    std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, int64_t);
+std::vector<at::Tensor> emb_pooled_scale(std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor,
+                                         std::vector<at::Tensor>, std::vector<at::Tensor>,
+                                         std::vector<at::Tensor>, at::Tensor, int64_t);
+void emb_reduce_update(std::vector<at::Tensor>, at::Tensor, std::vector<at::Tensor>, std::vector<at::Tensor>,
+                       std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, int64_t, at::Tensor,
+                       at::Tensor, c10::optional<at::Tensor>, c10::optional<at::Tensor>, int64_t, double,
+                       double, double, double, double, double, double, at::Tensor);
+// norm.cu
+std::vector<at::Tensor> norm_fwd(at::Tensor, c10::optional<at::Tensor>, at::Tensor, c10::optional<at::Tensor>,
+                                 double, int64_t);
+std::vector<at::Tensor> norm_bwd(at::Tensor, at::Tensor, c10::optional<at::Tensor>, at::Tensor, at::Tensor,
+                                 c10::optional<at::Tensor>, int64_t);
+// loss.cu
+std::vector<at::Tensor> heads_loss_fwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, std::vector<double>,
+                                       std::vector<int64_t>);
+std::vector<at::Tensor> heads_loss_bwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor);
+// optim.cu
+void grad_sqnorm(at::Tensor, at::Tensor);
+void adamw_step(at::Tensor, at::Tensor, at::Tensor, at::Tensor, double, double, double, double, double, double,
+                double, double, c10::optional<at::Tensor>);
+void scale_(at::Tensor, double);
+long long launches();
+}  // namespace pd
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "primus_dlrm_b200 sm_100a core kernels";
+  m.def("emb_gather", &pd::emb_gather);
+  m.def("emb_pooled", &pd::emb_pooled);
+  m.def("emb_keys", &pd::emb_keys);
+  m.def("emb_pooled_scale", &pd::emb_pooled_scale);
+  m.def("emb_reduce_update", &pd::emb_reduce_update);
+  m.def("norm_fwd", &pd::norm_fwd);
+  m.def("norm_bwd", &pd::norm_bwd);
+  m.def("heads_loss_fwd", &pd::heads_loss_fwd);
+  m.def("heads_loss_bwd", &pd::heads_loss_bwd);
+  m.def("grad_sqnorm", &pd::grad_sqnorm);
+  m.def("adamw_step", &pd::adamw_step);
+  m.def("scale_", &pd::scale_);
+  m.def("launch_count", &pd::launches, "kernels launched by this extension so far");
+}

@@ -1,0 +1,113 @@
+// Shared helpers for the sm_100a kernels of primus_dlrm_b200.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+// Light ATen headers only (no torch/extension.h): keeps nvcc host passes fast.
+#include <ATen/core/Tensor.h>
+#include <ATen/ops/empty.h>
+#include <ATen/ops/empty_like.h>
+#include <ATen/ops/zeros.h>
+#include <ATen/ops/zeros_like.h>
+#include <c10/cuda/CUDAStream.h>
+#include <c10/util/Exception.h>
+#include <atomic>
+#include <optional>
+#include <vector>
+
+#define PD_CHECK_CUDA(expr)                                                        \
+  do {                                                                             \
+    cudaError_t err__ = (expr);                                                    \
+    TORCH_CHECK(err__ == cudaSuccess, "CUDA error ", cudaGetErrorString(err__),    \
+                " at ", __FILE__, ":", __LINE__);                                  \
+  } while (0)
+
+#define PD_CHECK_LAUNCH() do { PD_CHECK_CUDA(cudaGetLastError()); ::pd::note_launch(); } while (0)
+
+namespace pd {
+
+// Error codes a kernel writes into the device error word instead of faulting.
+enum ErrorCode : int {
+  kOk = 0,
+  kIdOutOfRange = 1,
+  kWaitTimeout = 2,
+  kBadShape = 3,
+};
+
+// Number of kernels this library has launched (read by benchmarks to report
+// how many of their kernels ran inside a timed region).
+inline std::atomic<long long>& launch_counter() {
+  static std::atomic<long long> n{0};
+  return n;
+}
+inline void note_launch(int k = 1) { launch_counter().fetch_add(k, std::memory_order_relaxed); }
+
+inline cudaStream_t stream() { return c10::cuda::getCurrentCUDAStream().stream(); }
+
+inline int num_sms() {
+  static int n = -1;
+  if (n < 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+__device__ __forceinline__ float bf16_to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+__device__ __forceinline__ void store4_bf16(__nv_bfloat16* dst, float4 v) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
+  __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 pk;
+  pk.x = *reinterpret_cast<uint32_t*>(&a);
+  pk.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(dst) = pk;
+}
+
+__device__ __forceinline__ float4 load4_bf16(const __nv_bfloat16* src) {
+  uint2 pk = *reinterpret_cast<const uint2*>(src);
+  __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&pk.x);
+  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&pk.y);
+  float2 fa = __bfloat1622float2(a);
+  float2 fb = __bfloat1622float2(b);
+  return make_float4(fa.x, fa.y, fb.x, fb.y);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Record the first error code seen by any thread (never traps).
+__device__ __forceinline__ void set_error(int* err, int code) {
+  if (err != nullptr) atomicCAS(err, 0, code);
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// GELU (tanh-free exact form via erf), shared by epilogues and tokenizers.
+__device__ __forceinline__ float gelu_f(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+__device__ __forceinline__ float gelu_grad_f(float x) {
+  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752f));
+  const float pdf = 0.3989422804014327f * __expf(-0.5f * x * x);
+  return cdf + x * pdf;
+}
+
+}  // namespace pd

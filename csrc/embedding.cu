@@ -1,0 +1,687 @@
+// Embedding lookup and fused sparse-optimizer backward for sm_100a.
+//
+// Replaces the FBGEMM TBE forward/backward the reference reaches through
+// TorchRec (primus_dlrm/models/embedding.py:117-175 and the fused optimizer
+// registered at primus_dlrm/distributed/wrapper.py:151-174).
+//
+// Design:
+//  * One launch gathers every feature of one embedding dim. Each feature is a
+//    "slot": ids + an output view (base pointer already offset to the slot's
+//    column, row stride in elements). Writing a slot at column k*E of a
+//    [B, L, G*E] buffer fuses the per-pool torch.cat of the tokenizer input;
+//    writing bf16 fuses the autocast cast.
+//  * Tables are read through an array of row-shard base pointers. A table on
+//    one device has one shard. A row-wise sharded table has one shard per
+//    rank, mapped into this process over NVLink (CUDA IPC), so the same
+//    kernel is the cross-GPU lookup: rows are pulled straight from the
+//    owner's HBM with peer loads, no id or row all-to-all.
+//  * Backward sorts (table, row) keys, then one warp per chunk of 32 sorted
+//    positions reduces each run of equal keys in registers and applies the
+//    optimizer (SGD / Adagrad / row-wise Adagrad / Adam) to the touched row.
+//    A run that crosses a chunk boundary (a hot Zipf row) is reduced by
+//    every chunk it touches into a scratch row with fp32 atomics; the last
+//    chunk to finish (per-row arrival counter) applies the update and clears
+//    the scratch row and counter, so the scratch stays zero between calls.
+//  * Nothing traps: an out-of-range id writes a zero row and records
+//    kIdOutOfRange in the error word.
+#include "common.cuh"
+
+namespace pd {
+
+constexpr int kMaxSlots = 48;
+constexpr int kMaxTables = 24;
+constexpr int kChunk = 32;  // sorted positions per warp in the backward
+
+struct Slot {
+  const void* ids;          // int32 or int64 ids, [n]
+  void* io;                 // fwd: output view base; bwd: grad view base
+  const int64_t* offsets;   // pooled jagged bags: [n_bags + 1]; nullptr = fixed bags
+  int64_t n;                // number of ids
+  int64_t io_stride;        // elements between consecutive output rows
+  int32_t table;
+  int32_t pool;             // 0 none, 1 sum, 2 mean
+  int32_t bag_len;          // fixed bag length when pooled and offsets == nullptr
+  int32_t pad_id;           // pooled: id excluded from the bag (-1 = none)
+  int64_t n_bags;           // pooled: number of bags
+};
+
+struct Table {
+  const float* const* shards;  // [n_shards] row-shard base pointers (device array)
+  float* local;                // this rank's shard (updated in backward)
+  float* state1;               // rowwise/adagrad accumulator or Adam m
+  float* state2;               // Adam v
+  int64_t rows;                // global rows
+  int64_t chunk;               // rows per shard
+  int64_t key_base;            // first sort key of this table
+  int64_t local_row0;          // first global row owned by this rank
+  int64_t local_rows;          // rows in this rank's shard
+  int32_t n_shards;
+  int32_t dim;
+};
+
+struct GatherParams {
+  Slot slots[kMaxSlots];
+  int64_t slot_off[kMaxSlots + 1];
+  int64_t bag_off[kMaxSlots + 1];  // pooled: prefix of bag counts over slots
+  Table tables[kMaxTables];
+  int n_slots;
+  int n_tables;
+  int dim;
+};
+
+template <typename IdT>
+__device__ __forceinline__ int64_t load_id(const void* p, int64_t i) {
+  return static_cast<int64_t>(static_cast<const IdT*>(p)[i]);
+}
+
+__device__ __forceinline__ int find_slot(const int64_t* off, int n, int64_t p) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (off[mid] <= p) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Resolve a global row of table t to a readable pointer (local or peer).
+__device__ __forceinline__ const float* row_ptr(const Table& t, int64_t g, bool& ok) {
+  ok = (g >= 0 && g < t.rows);
+  if (!ok) return nullptr;
+  int64_t owner = g / t.chunk;
+  if (owner >= t.n_shards) owner = t.n_shards - 1;
+  const int64_t r = g - owner * t.chunk;
+  return t.shards[owner] + r * t.dim;
+}
+
+// ---------------------------------------------------------------------------
+// Unpooled gather: out[slot][i] = W[table][ids[i]]
+// Threads of a warp split into groups of `lanes` threads, each group owning a
+// row; each thread moves `vpt` float4 of the row.
+// ---------------------------------------------------------------------------
+template <typename IdT, typename OutT>
+__global__ void __launch_bounds__(256) gather_kernel(const __grid_constant__ GatherParams P,
+                                                     int64_t total, int* err) {
+  const int nvec = P.dim >> 2;
+  const int lanes = nvec < 32 ? nvec : 32;
+  const int groups_per_warp = 32 / lanes;
+  const int lane = threadIdx.x & 31;
+  const int grp = lane / lanes;
+  const int sub = lane % lanes;
+  if (grp >= groups_per_warp) return;
+  const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t r = warp_global * groups_per_warp + grp; r < total; r += n_warps * groups_per_warp) {
+    const int s = find_slot(P.slot_off, P.n_slots, r);
+    const Slot& sl = P.slots[s];
+    const int64_t i = r - P.slot_off[s];
+    const int64_t g = load_id<IdT>(sl.ids, i);
+    bool ok;
+    const float* src = row_ptr(P.tables[sl.table], g, ok);
+    OutT* dst = static_cast<OutT*>(sl.io) + i * sl.io_stride;
+    if (!ok && sub == 0) set_error(err, kIdOutOfRange);
+    for (int v = sub; v < nvec; v += lanes) {
+      float4 x = ok ? __ldg(reinterpret_cast<const float4*>(src) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if constexpr (std::is_same<OutT, float>::value) {
+        reinterpret_cast<float4*>(dst)[v] = x;
+      } else {
+        store4_bf16(dst + 4 * v, x);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Pooled gather (sum / mean over a bag, pad id excluded): one warp per bag.
+// ---------------------------------------------------------------------------
+template <typename IdT, typename OutT>
+__global__ void __launch_bounds__(256) pooled_kernel(const __grid_constant__ GatherParams P,
+                                                     int64_t total_bags, int* err) {
+  const int64_t* bag_off = P.bag_off;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  const int nvec = P.dim >> 2;
+  for (int64_t b = warp_global; b < total_bags; b += n_warps) {
+    const int s = find_slot(bag_off, P.n_slots, b);
+    const Slot& sl = P.slots[s];
+    const int64_t bag = b - bag_off[s];
+    int64_t beg, end;
+    if (sl.offsets) { beg = sl.offsets[bag]; end = sl.offsets[bag + 1]; }
+    else { beg = bag * sl.bag_len; end = beg + sl.bag_len; }
+    const Table& t = P.tables[sl.table];
+    float4 acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    int cnt = 0;
+    for (int64_t j = beg; j < end; ++j) {
+      const int64_t g = load_id<IdT>(sl.ids, j);
+      if (g == sl.pad_id) continue;
+      bool ok;
+      const float* src = row_ptr(t, g, ok);
+      if (!ok) { if (lane == 0) set_error(err, kIdOutOfRange); continue; }
+      ++cnt;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int v = lane + 32 * k;
+        if (v < nvec) {
+          float4 x = __ldg(reinterpret_cast<const float4*>(src) + v);
+          acc[k].x += x.x; acc[k].y += x.y; acc[k].z += x.z; acc[k].w += x.w;
+        }
+      }
+    }
+    const float sc = (sl.pool == 2 && cnt > 0) ? 1.f / cnt : 1.f;
+    OutT* dst = static_cast<OutT*>(sl.io) + bag * sl.io_stride;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int v = lane + 32 * k;
+      if (v < nvec) {
+        float4 x = make_float4(acc[k].x * sc, acc[k].y * sc, acc[k].z * sc, acc[k].w * sc);
+        if constexpr (std::is_same<OutT, float>::value) reinterpret_cast<float4*>(dst)[v] = x;
+        else store4_bf16(dst + 4 * v, x);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward step 1: sort keys. key = table.key_base + global row; positions
+// that contribute nothing (pooled pad ids, out-of-range ids) get INT64_MAX.
+// ---------------------------------------------------------------------------
+template <typename IdT>
+__global__ void keys_kernel(const __grid_constant__ GatherParams P, int64_t total, int64_t* keys) {
+  for (int64_t p = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; p < total;
+       p += int64_t(gridDim.x) * blockDim.x) {
+    const int s = find_slot(P.slot_off, P.n_slots, p);
+    const Slot& sl = P.slots[s];
+    const int64_t g = load_id<IdT>(sl.ids, p - P.slot_off[s]);
+    const Table& t = P.tables[sl.table];
+    const bool skip = (sl.pool != 0 && g == sl.pad_id) || g < 0 || g >= t.rows;
+    keys[p] = skip ? INT64_MAX : t.key_base + g;
+  }
+}
+
+// Per-position gradient scale and row for pooled slots (bag -> row, 1/count).
+template <typename IdT>
+__global__ void pooled_scale_kernel(const __grid_constant__ GatherParams P, int64_t total,
+                                    float* scale, int64_t* grad_row) {
+  for (int64_t p = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; p < total;
+       p += int64_t(gridDim.x) * blockDim.x) {
+    const int s = find_slot(P.slot_off, P.n_slots, p);
+    const Slot& sl = P.slots[s];
+    const int64_t i = p - P.slot_off[s];
+    if (sl.pool == 0) { scale[p] = 1.f; grad_row[p] = i; continue; }
+    int64_t bag, beg, end;
+    if (sl.offsets) {
+      int64_t lo = 0, hi = sl.n_bags - 1;
+      while (lo < hi) { int64_t m = (lo + hi + 1) >> 1; if (sl.offsets[m] <= i) lo = m; else hi = m - 1; }
+      bag = lo; beg = sl.offsets[bag]; end = sl.offsets[bag + 1];
+    } else {
+      bag = i / sl.bag_len; beg = bag * sl.bag_len; end = beg + sl.bag_len;
+    }
+    float sc = 1.f;
+    if (sl.pool == 2) {
+      int cnt = 0;
+      for (int64_t j = beg; j < end; ++j) cnt += (load_id<IdT>(sl.ids, j) != sl.pad_id);
+      sc = cnt > 0 ? 1.f / cnt : 0.f;
+    }
+    scale[p] = sc;
+    grad_row[p] = bag;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward step 2: reduce runs of equal sorted keys + apply the optimizer.
+// ---------------------------------------------------------------------------
+struct OptParams {
+  int kind;        // 0 sgd, 1 adagrad, 2 rowwise_adagrad, 3 adam
+  float lr;
+  float eps;
+  float weight_decay;
+  float beta1, beta2;
+  float bc1, bc2;  // Adam bias corrections 1 - beta^t
+};
+
+// Grad source: sorted position q -> (slot via perm) -> grad row pointer.
+struct GradSrc {
+  const int64_t* perm;      // sorted q -> original position p
+  const float* scale;       // per original position (pooled); nullptr = 1
+  const int64_t* grad_row;  // per original position: row within the slot's grad view; nullptr = i
+};
+
+template <typename GradT>
+__device__ __forceinline__ void accum_row(float4* acc, const GradT* src, int nvec, int lane, float sc) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int v = lane + 32 * k;
+    if (v < nvec) {
+      float4 x;
+      if constexpr (std::is_same<GradT, float>::value) x = reinterpret_cast<const float4*>(src)[v];
+      else x = load4_bf16(src + 4 * v);
+      acc[k].x += sc * x.x; acc[k].y += sc * x.y; acc[k].z += sc * x.z; acc[k].w += sc * x.w;
+    }
+  }
+}
+
+__device__ __forceinline__ int find_table(const GatherParams& P, int64_t key) {
+  int lo = 0, hi = P.n_tables - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (P.tables[mid].key_base <= key) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Apply the optimizer to one row (this rank owns it). acc holds the summed grad.
+__device__ void apply_update(const GatherParams& P, const OptParams& O, int64_t key,
+                             float4* acc, int nvec, int lane, int* err) {
+  const int ti = find_table(P, key);
+  const Table& t = P.tables[ti];
+  const int64_t g = key - t.key_base;
+  const int64_t r = g - t.local_row0;
+  if (r < 0 || r >= t.local_rows) { if (lane == 0) set_error(err, kIdOutOfRange); return; }
+  float4* w = reinterpret_cast<float4*>(t.local + r * t.dim);
+  float4 wv[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int v = lane + 32 * k;
+    wv[k] = v < nvec ? w[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (O.weight_decay != 0.f && v < nvec) {
+      acc[k].x += O.weight_decay * wv[k].x; acc[k].y += O.weight_decay * wv[k].y;
+      acc[k].z += O.weight_decay * wv[k].z; acc[k].w += O.weight_decay * wv[k].w;
+    }
+  }
+  if (O.kind == 2) {  // row-wise Adagrad: one accumulator per row, mean of g^2
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (lane + 32 * k < nvec)
+        ss += acc[k].x * acc[k].x + acc[k].y * acc[k].y + acc[k].z * acc[k].z + acc[k].w * acc[k].w;
+    ss = warp_sum(ss) / float(t.dim);
+    float G = 0.f;
+    if (lane == 0) { G = t.state1[r] + ss; t.state1[r] = G; }
+    G = __shfl_sync(0xffffffffu, G, 0);
+    const float mul = O.lr / (sqrtf(G) + O.eps);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int v = lane + 32 * k;
+      if (v < nvec) {
+        wv[k].x -= mul * acc[k].x; wv[k].y -= mul * acc[k].y;
+        wv[k].z -= mul * acc[k].z; wv[k].w -= mul * acc[k].w;
+        w[v] = wv[k];
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int v = lane + 32 * k;
+    if (v >= nvec) continue;
+    float* gp = reinterpret_cast<float*>(&acc[k]);
+    float* wp = reinterpret_cast<float*>(&wv[k]);
+    if (O.kind == 0) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) wp[e] -= O.lr * gp[e];
+    } else if (O.kind == 1) {
+      float4 s = reinterpret_cast<float4*>(t.state1 + r * t.dim)[v];
+      float* sp = reinterpret_cast<float*>(&s);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) { sp[e] += gp[e] * gp[e]; wp[e] -= O.lr * gp[e] / (sqrtf(sp[e]) + O.eps); }
+      reinterpret_cast<float4*>(t.state1 + r * t.dim)[v] = s;
+    } else {
+      float4 m = reinterpret_cast<float4*>(t.state1 + r * t.dim)[v];
+      float4 vv = reinterpret_cast<float4*>(t.state2 + r * t.dim)[v];
+      float* mp = reinterpret_cast<float*>(&m);
+      float* vp = reinterpret_cast<float*>(&vv);
+      const float step = O.lr / O.bc1;
+      const float inv_sqrt_bc2 = rsqrtf(O.bc2);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        mp[e] = O.beta1 * mp[e] + (1.f - O.beta1) * gp[e];
+        vp[e] = O.beta2 * vp[e] + (1.f - O.beta2) * gp[e] * gp[e];
+        wp[e] -= step * mp[e] / (sqrtf(vp[e]) * inv_sqrt_bc2 + O.eps);
+      }
+      reinterpret_cast<float4*>(t.state1 + r * t.dim)[v] = m;
+      reinterpret_cast<float4*>(t.state2 + r * t.dim)[v] = vv;
+    }
+    w[v] = wv[k];
+  }
+}
+
+__device__ __forceinline__ int64_t lower_bound(const int64_t* a, int64_t n, int64_t key) {
+  int64_t lo = 0, hi = n;
+  while (lo < hi) { int64_t m = (lo + hi) >> 1; if (a[m] < key) lo = m + 1; else hi = m; }
+  return lo;
+}
+
+// GradT: dtype of the grad views. Positions index the slots of P (or a flat
+// receive buffer when P.n_slots == 1 and the slot covers it).
+template <typename GradT>
+__global__ void __launch_bounds__(256) reduce_update_kernel(
+    const __grid_constant__ GatherParams P, OptParams O, const int64_t* __restrict__ skeys,
+    GradSrc src, int64_t total, float* __restrict__ scratch, int* __restrict__ arrivals, int* err) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = P.dim >> 2;
+  const int64_t n_chunks = (total + kChunk - 1) / kChunk;
+  const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t c = warp_global; c < n_chunks; c += n_warps) {
+    const int64_t c0 = c * kChunk;
+    const int64_t c1 = min(c0 + kChunk, total);
+    int64_t a = c0;
+    while (a < c1) {
+      const int64_t key = skeys[a];
+      if (key == INT64_MAX) break;  // sentinel tail
+      int64_t b = a + 1;
+      while (b < c1 && skeys[b] == key) ++b;
+      float4 acc[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int64_t q = a; q < b; ++q) {
+        const int64_t p = src.perm[q];
+        const int s = find_slot(P.slot_off, P.n_slots, p);
+        const Slot& sl = P.slots[s];
+        const int64_t i = p - P.slot_off[s];
+        const int64_t row = src.grad_row ? src.grad_row[p] : i;
+        const float sc = src.scale ? src.scale[p] : 1.f;
+        accum_row<GradT>(acc, static_cast<const GradT*>(sl.io) + row * sl.io_stride, nvec, lane, sc);
+      }
+      const bool head = (a > 0) ? (skeys[a - 1] != key) : true;
+      const bool tail = (b < total) ? (skeys[b] != key) : true;
+      if (head && tail) {
+        apply_update(P, O, key, acc, nvec, lane, err);
+      } else {
+        // The run spans several chunks: accumulate into the head chunk's
+        // scratch row; the last arriving chunk applies the update.
+        const int64_t beg = head ? a : lower_bound(skeys, total, key);
+        const int64_t end = tail ? b : lower_bound(skeys, total, key + 1);
+        const int64_t hc = beg / kChunk;
+        const int span = int((end - 1) / kChunk - hc + 1);
+        float* srow = scratch + hc * int64_t(P.dim);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int v = lane + 32 * k;
+          if (v < nvec) {
+            atomicAdd(srow + 4 * v + 0, acc[k].x); atomicAdd(srow + 4 * v + 1, acc[k].y);
+            atomicAdd(srow + 4 * v + 2, acc[k].z); atomicAdd(srow + 4 * v + 3, acc[k].w);
+          }
+        }
+        __threadfence();
+        __syncwarp();
+        int prev = 0;
+        if (lane == 0) prev = atomicAdd(arrivals + hc, 1);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == span - 1) {
+          __threadfence();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int v = lane + 32 * k;
+            if (v < nvec) {
+              acc[k] = __ldcg(reinterpret_cast<const float4*>(srow) + v);
+              reinterpret_cast<float4*>(srow)[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
+          if (lane == 0) arrivals[hc] = 0;
+          apply_update(P, O, key, acc, nvec, lane, err);
+        }
+      }
+      a = b;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+static int64_t grid_for(int64_t work_items, int per_block) {
+  int64_t blocks = (work_items + per_block - 1) / per_block;
+  const int64_t cap = int64_t(num_sms()) * 16;
+  if (blocks > cap) blocks = cap;
+  return blocks < 1 ? 1 : blocks;
+}
+
+// tables: list of [weight(local shard, fp32 2D), shard_ptrs(int64 device tensor),
+//          state1, state2] packed as tensors; meta: int64 [n_tables, 6] CPU tensor
+//          (rows, chunk, key_base, local_row0, n_shards, dim).
+static void fill_tables(GatherParams& P, const std::vector<at::Tensor>& weights,
+                        const std::vector<at::Tensor>& shard_ptrs,
+                        const std::vector<at::Tensor>& state1,
+                        const std::vector<at::Tensor>& state2, const at::Tensor& meta) {
+  const int nt = static_cast<int>(weights.size());
+  TORCH_CHECK(nt <= kMaxTables, "too many tables in one launch: ", nt);
+  TORCH_CHECK(meta.device().is_cpu() && meta.dtype() == at::kLong && meta.size(0) == nt && meta.size(1) == 6);
+  auto m = meta.accessor<int64_t, 2>();
+  P.n_tables = nt;
+  for (int t = 0; t < nt; ++t) {
+    Table& T = P.tables[t];
+    TORCH_CHECK(weights[t].dtype() == at::kFloat && weights[t].is_contiguous(), "table must be fp32 contiguous");
+    TORCH_CHECK(shard_ptrs[t].is_cuda() && shard_ptrs[t].dtype() == at::kLong);
+    T.shards = reinterpret_cast<const float* const*>(shard_ptrs[t].data_ptr<int64_t>());
+    T.local = weights[t].data_ptr<float>();
+    T.state1 = state1[t].numel() ? state1[t].data_ptr<float>() : nullptr;
+    T.state2 = state2[t].numel() ? state2[t].data_ptr<float>() : nullptr;
+    T.rows = m[t][0]; T.chunk = m[t][1]; T.key_base = m[t][2];
+    T.local_row0 = m[t][3]; T.n_shards = int(m[t][4]); T.dim = int(m[t][5]);
+    TORCH_CHECK(T.dim == P.dim, "all tables of one launch must share the embedding dim");
+    TORCH_CHECK(T.chunk > 0 && T.n_shards >= 1 && shard_ptrs[t].numel() == T.n_shards);
+  }
+}
+
+static at::ScalarType fill_slots(GatherParams& P, const std::vector<at::Tensor>& ids,
+                                 const std::vector<at::Tensor>& io, const at::Tensor& slot_meta,
+                                 const std::vector<at::Tensor>& offsets, bool pooled_allowed) {
+  const int ns = static_cast<int>(ids.size());
+  TORCH_CHECK(ns >= 1 && ns <= kMaxSlots, "slot count out of range: ", ns);
+  TORCH_CHECK(io.size() == ids.size());
+  TORCH_CHECK(slot_meta.device().is_cpu() && slot_meta.dtype() == at::kLong &&
+              slot_meta.size(0) == ns && slot_meta.size(1) == 4);
+  auto sm = slot_meta.accessor<int64_t, 2>();  // table, pool, bag_len, pad_id
+  const at::ScalarType id_t = ids[0].scalar_type();
+  P.n_slots = ns;
+  P.slot_off[0] = 0;
+  for (int s = 0; s < ns; ++s) {
+    Slot& S = P.slots[s];
+    TORCH_CHECK(ids[s].scalar_type() == id_t, "ids of one launch must share a dtype");
+    TORCH_CHECK(id_t == at::kInt || id_t == at::kLong, "ids must be int32 or int64");
+    TORCH_CHECK(ids[s].is_contiguous());
+    TORCH_CHECK(io[s].dim() == 2 && io[s].stride(1) == 1 && io[s].size(1) == P.dim,
+                "io view must be [rows, dim] with unit column stride");
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(io[s].data_ptr()) % 8) == 0 && io[s].stride(0) % 4 == 0,
+                "io view must be 8-byte aligned with a row stride multiple of 4");
+    S.ids = ids[s].data_ptr();
+    S.io = io[s].data_ptr();
+    S.n = ids[s].numel();
+    S.io_stride = io[s].stride(0);
+    S.table = int(sm[s][0]);
+    S.pool = int(sm[s][1]);
+    S.bag_len = int(sm[s][2]);
+    S.pad_id = int(sm[s][3]);
+    TORCH_CHECK(S.table >= 0 && S.table < P.n_tables);
+    TORCH_CHECK(pooled_allowed || S.pool == 0);
+    S.offsets = (offsets.size() > size_t(s) && offsets[s].numel()) ? offsets[s].data_ptr<int64_t>() : nullptr;
+    if (S.pool) {
+      S.n_bags = S.offsets ? offsets[s].numel() - 1 : (S.bag_len > 0 ? S.n / S.bag_len : 0);
+      TORCH_CHECK(io[s].size(0) == S.n_bags, "pooled output rows must equal bag count");
+    } else {
+      S.n_bags = 0;
+      TORCH_CHECK(io[s].size(0) == S.n, "unpooled output rows must equal id count");
+    }
+    P.slot_off[s + 1] = P.slot_off[s] + S.n;
+  }
+  return id_t;
+}
+
+// Forward gather (unpooled slots).
+void emb_gather(std::vector<at::Tensor> ids, std::vector<at::Tensor> outs, at::Tensor slot_meta,
+                std::vector<at::Tensor> weights, std::vector<at::Tensor> shard_ptrs,
+                at::Tensor table_meta, int64_t dim, at::Tensor err) {
+  GatherParams P;
+  P.dim = int(dim);
+  TORCH_CHECK(dim % 4 == 0 && dim <= 1024, "embedding dim must be a multiple of 4 and <= 1024");
+  std::vector<at::Tensor> e1;
+  for (size_t i = 0; i < weights.size(); ++i) e1.push_back(at::empty({0}, weights[i].options()));
+  fill_tables(P, weights, shard_ptrs, e1, e1, table_meta);
+  const auto id_t = fill_slots(P, ids, outs, slot_meta, {}, false);
+  const int64_t total = P.slot_off[P.n_slots];
+  if (total == 0) return;
+  const at::ScalarType out_t = outs[0].scalar_type();
+  for (auto& o : outs) TORCH_CHECK(o.scalar_type() == out_t, "outputs of one launch must share a dtype");
+  const int nvec = P.dim / 4;
+  const int rows_per_warp = nvec < 32 ? 32 / nvec : 1;
+  const int64_t blocks = grid_for((total + 8 * rows_per_warp - 1) / (8 * rows_per_warp), 1);
+  int* e = err.data_ptr<int>();
+  auto s = stream();
+#define PD_LAUNCH_GATHER(IDT, OT) gather_kernel<IDT, OT><<<blocks, 256, 0, s>>>(P, total, e)
+  if (id_t == at::kInt) {
+    if (out_t == at::kBFloat16) PD_LAUNCH_GATHER(int32_t, __nv_bfloat16); else PD_LAUNCH_GATHER(int32_t, float);
+  } else {
+    if (out_t == at::kBFloat16) PD_LAUNCH_GATHER(int64_t, __nv_bfloat16); else PD_LAUNCH_GATHER(int64_t, float);
+  }
+#undef PD_LAUNCH_GATHER
+  PD_CHECK_LAUNCH();
+}
+
+// Forward pooled gather (sum/mean bags).
+void emb_pooled(std::vector<at::Tensor> ids, std::vector<at::Tensor> outs, at::Tensor slot_meta,
+                std::vector<at::Tensor> offsets, std::vector<at::Tensor> weights,
+                std::vector<at::Tensor> shard_ptrs, at::Tensor table_meta, int64_t dim, at::Tensor err) {
+  GatherParams P;
+  P.dim = int(dim);
+  TORCH_CHECK(dim % 4 == 0 && dim <= 1024);
+  std::vector<at::Tensor> e1;
+  for (size_t i = 0; i < weights.size(); ++i) e1.push_back(at::empty({0}, weights[i].options()));
+  fill_tables(P, weights, shard_ptrs, e1, e1, table_meta);
+  const auto id_t = fill_slots(P, ids, outs, slot_meta, offsets, true);
+  // bag offsets over slots (slot bag counts are known on the host)
+  P.bag_off[0] = 0;
+  for (int s = 0; s < P.n_slots; ++s) P.bag_off[s + 1] = P.bag_off[s] + P.slots[s].n_bags;
+  const int64_t total_bags = P.bag_off[P.n_slots];
+  if (total_bags == 0) return;
+  const at::ScalarType out_t = outs[0].scalar_type();
+  const int64_t blocks = grid_for((total_bags + 7) / 8, 1);
+  int* e = err.data_ptr<int>();
+  auto s = stream();
+#define PD_LAUNCH_POOL(IDT, OT) \
+  pooled_kernel<IDT, OT><<<blocks, 256, 0, s>>>(P, total_bags, e)
+  if (id_t == at::kInt) {
+    if (out_t == at::kBFloat16) PD_LAUNCH_POOL(int32_t, __nv_bfloat16); else PD_LAUNCH_POOL(int32_t, float);
+  } else {
+    if (out_t == at::kBFloat16) PD_LAUNCH_POOL(int64_t, __nv_bfloat16); else PD_LAUNCH_POOL(int64_t, float);
+  }
+#undef PD_LAUNCH_POOL
+  PD_CHECK_LAUNCH();
+}
+
+// Sort keys for the backward (one key per id position over all slots).
+at::Tensor emb_keys(std::vector<at::Tensor> ids, std::vector<at::Tensor> grads, at::Tensor slot_meta,
+                    std::vector<at::Tensor> offsets, std::vector<at::Tensor> weights,
+                    std::vector<at::Tensor> shard_ptrs, at::Tensor table_meta, int64_t dim) {
+  GatherParams P;
+  P.dim = int(dim);
+  std::vector<at::Tensor> e1;
+  for (size_t i = 0; i < weights.size(); ++i) e1.push_back(at::empty({0}, weights[i].options()));
+  fill_tables(P, weights, shard_ptrs, e1, e1, table_meta);
+  const auto id_t = fill_slots(P, ids, grads, slot_meta, offsets, true);
+  const int64_t total = P.slot_off[P.n_slots];
+  auto keys = at::empty({total}, ids[0].options().dtype(at::kLong));
+  if (total == 0) return keys;
+  const int64_t blocks = grid_for(total, 256);
+  if (id_t == at::kInt) keys_kernel<int32_t><<<blocks, 256, 0, stream()>>>(P, total, keys.data_ptr<int64_t>());
+  else keys_kernel<int64_t><<<blocks, 256, 0, stream()>>>(P, total, keys.data_ptr<int64_t>());
+  PD_CHECK_LAUNCH();
+  return keys;
+}
+
+// Per-position scale/row for pooled slots: returns (scale f32 [N], grad_row i64 [N]).
+std::vector<at::Tensor> emb_pooled_scale(std::vector<at::Tensor> ids, std::vector<at::Tensor> grads,
+                                         at::Tensor slot_meta, std::vector<at::Tensor> offsets,
+                                         std::vector<at::Tensor> weights,
+                                         std::vector<at::Tensor> shard_ptrs, at::Tensor table_meta,
+                                         int64_t dim) {
+  GatherParams P;
+  P.dim = int(dim);
+  std::vector<at::Tensor> e1;
+  for (size_t i = 0; i < weights.size(); ++i) e1.push_back(at::empty({0}, weights[i].options()));
+  fill_tables(P, weights, shard_ptrs, e1, e1, table_meta);
+  const auto id_t = fill_slots(P, ids, grads, slot_meta, offsets, true);
+  const int64_t total = P.slot_off[P.n_slots];
+  auto scale = at::empty({total}, ids[0].options().dtype(at::kFloat));
+  auto row = at::empty({total}, ids[0].options().dtype(at::kLong));
+  if (total == 0) return {scale, row};
+  const int64_t blocks = grid_for(total, 256);
+  if (id_t == at::kInt)
+    pooled_scale_kernel<int32_t><<<blocks, 256, 0, stream()>>>(P, total, scale.data_ptr<float>(), row.data_ptr<int64_t>());
+  else
+    pooled_scale_kernel<int64_t><<<blocks, 256, 0, stream()>>>(P, total, scale.data_ptr<float>(), row.data_ptr<int64_t>());
+  PD_CHECK_LAUNCH();
+  return {scale, row};
+}
+
+// Scratch for runs that cross chunk boundaries: one fp32 row and one arrival
+// counter per chunk. Kept zero between calls by the kernel itself.
+struct ScratchCache {
+  at::Tensor rows, arrivals;
+};
+static ScratchCache& scratch_for(int device) {
+  static ScratchCache caches[64];
+  return caches[device];
+}
+
+void emb_reduce_update(std::vector<at::Tensor> grads, at::Tensor slot_meta,
+                       std::vector<at::Tensor> weights, std::vector<at::Tensor> shard_ptrs,
+                       std::vector<at::Tensor> state1, std::vector<at::Tensor> state2,
+                       at::Tensor table_meta, int64_t dim, at::Tensor sorted_keys, at::Tensor perm,
+                       c10::optional<at::Tensor> scale, c10::optional<at::Tensor> grad_row,
+                       int64_t opt_kind, double lr, double eps, double weight_decay, double beta1,
+                       double beta2, double bc1, double bc2, at::Tensor err) {
+  GatherParams P;
+  P.dim = int(dim);
+  fill_tables(P, weights, shard_ptrs, state1, state2, table_meta);
+  // grads are described as slots whose ids are unused here: use the sorted
+  // keys tensor as a dummy id array of the right length per slot.
+  const int ns = int(grads.size());
+  TORCH_CHECK(ns >= 1 && ns <= kMaxSlots);
+  auto sm = slot_meta.accessor<int64_t, 2>();
+  P.n_slots = ns;
+  P.slot_off[0] = 0;
+  TORCH_CHECK(slot_meta.size(1) == 5, "slot_meta for reduce_update: table, pool, bag_len, pad, n_ids");
+  for (int s = 0; s < ns; ++s) {
+    Slot& S = P.slots[s];
+    TORCH_CHECK(grads[s].dim() == 2 && grads[s].stride(1) == 1 && grads[s].size(1) == dim);
+    S.ids = nullptr;
+    S.io = grads[s].data_ptr();
+    S.io_stride = grads[s].stride(0);
+    S.table = int(sm[s][0]); S.pool = int(sm[s][1]); S.bag_len = int(sm[s][2]); S.pad_id = int(sm[s][3]);
+    S.n = sm[s][4];
+    S.offsets = nullptr; S.n_bags = 0;
+    P.slot_off[s + 1] = P.slot_off[s] + S.n;
+  }
+  const int64_t total = P.slot_off[ns];
+  TORCH_CHECK(sorted_keys.numel() == total && perm.numel() == total);
+  if (total == 0) return;
+  const at::ScalarType gt = grads[0].scalar_type();
+  for (auto& g : grads) TORCH_CHECK(g.scalar_type() == gt);
+  OptParams O{int(opt_kind), float(lr), float(eps), float(weight_decay), float(beta1), float(beta2),
+              float(bc1), float(bc2)};
+  GradSrc src{perm.data_ptr<int64_t>(), scale ? scale->data_ptr<float>() : nullptr,
+              grad_row ? grad_row->data_ptr<int64_t>() : nullptr};
+  const int64_t n_chunks = (total + kChunk - 1) / kChunk;
+  const int dev = weights[0].get_device();
+  ScratchCache& sc = scratch_for(dev);
+  if (!sc.rows.defined() || sc.rows.numel() < n_chunks * dim) {
+    sc.rows = at::zeros({n_chunks * dim + dim}, weights[0].options());
+    sc.arrivals = at::zeros({n_chunks + 1}, weights[0].options().dtype(at::kInt));
+  }
+  const int64_t blocks = grid_for((n_chunks + 7) / 8, 1);
+  if (gt == at::kBFloat16)
+    reduce_update_kernel<__nv_bfloat16><<<blocks, 256, 0, stream()>>>(
+        P, O, sorted_keys.data_ptr<int64_t>(), src, total, sc.rows.data_ptr<float>(),
+        sc.arrivals.data_ptr<int>(), err.data_ptr<int>());
+  else
+    reduce_update_kernel<float><<<blocks, 256, 0, stream()>>>(
+        P, O, sorted_keys.data_ptr<int64_t>(), src, total, sc.rows.data_ptr<float>(),
+        sc.arrivals.data_ptr<int>(), err.data_ptr<int>());
+  PD_CHECK_LAUNCH();
+}
+
+}  // namespace pd

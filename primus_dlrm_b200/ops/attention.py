@@ -1,0 +1,71 @@
+"""Pyramid causal attention.
+
+Semantics (``primus_dlrm/models/onetrans.py:62-67,146-166``): queries are the
+last ``q_len`` of ``kv_len`` tokens and attend causally with the mask aligned
+bottom-right, ``kv_idx <= q_idx + (kv_len - q_len)``; scale ``1/sqrt(d)``.
+
+Inputs are ``[B, L, H, d]`` views (any row stride, unit stride on ``d``);
+the output is ``[B, q_len, H, d]`` contiguous.
+
+Paths:
+* ``native`` -- the sm_100a pyramid FMHA in ``_gemm`` when built and the
+  shape is supported;
+* ``sdpa`` -- ``F.scaled_dot_product_attention`` with a lower-right causal
+  bias (flash / efficient backends);
+* ``mask`` -- SDPA with an explicit boolean mask (reference ``sdpa`` path).
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from primus_dlrm_b200.ops import _ext
+
+
+def build_pyramid_mask(q_len: int, kv_len: int, device) -> torch.Tensor:
+    """Boolean ``[q_len, kv_len]`` mask, True where attention is allowed."""
+    off = kv_len - q_len
+    qi = torch.arange(q_len, device=device).unsqueeze(1) + off
+    ki = torch.arange(kv_len, device=device).unsqueeze(0)
+    return ki <= qi
+
+
+def _native_ok(q: torch.Tensor) -> bool:
+    g = _ext.gemm() if (q.is_cuda and _ext.native_enabled(q.device)) else None
+    return g is not None and hasattr(g, "fmha_fwd") and q.dtype == torch.bfloat16 and q.shape[-1] in (32, 64)
+
+
+class _NativeFMHA(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, scale):
+        G = _ext.gemm()
+        o, lse = G.fmha_fwd(q, k, v, scale)
+        ctx.scale = scale
+        ctx.save_for_backward(q, k, v, o, lse)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        G = _ext.gemm()
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = G.fmha_bwd(q, k, v, o, lse, do.contiguous(), ctx.scale)
+        return dq, dk, dv, None
+
+
+def pyramid_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, impl: str = "auto",
+                      dropout_p: float = 0.0) -> torch.Tensor:
+    """q [B, q_len, H, d]; k, v [B, kv_len, H, d] -> [B, q_len, H, d]."""
+    B, ql, H, d = q.shape
+    kl = k.shape[1]
+    scale = d ** -0.5
+    if impl in ("auto", "native") and dropout_p == 0.0 and _native_ok(q):
+        return _NativeFMHA.apply(q, k, v, scale)
+    qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    if impl == "mask" or not q.is_cuda:
+        mask = build_pyramid_mask(ql, kl, q.device)
+        out = F.scaled_dot_product_attention(qt, kt, vt, attn_mask=mask, dropout_p=dropout_p)
+    else:
+        from torch.nn.attention.bias import causal_lower_right
+        out = F.scaled_dot_product_attention(qt, kt, vt, attn_mask=causal_lower_right(ql, kl),
+                                             dropout_p=dropout_p)
+    return out.transpose(1, 2).contiguous()

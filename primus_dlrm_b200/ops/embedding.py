@@ -1,0 +1,378 @@
+"""Embedding lookup with the sparse optimizer fused into its backward.
+
+The reference reaches this through TorchRec EC/EBC + FBGEMM TBE with
+``_apply_optimizer_in_backward`` (``primus_dlrm/models/embedding.py:72-175``,
+``primus_dlrm/distributed/wrapper.py:151-174``): embedding weights are never
+seen by the dense optimizer; the backward of the lookup updates the touched
+rows in place with Adam or row-wise Adagrad.
+
+Here one autograd node covers every feature of a lookup:
+
+* forward -- one ``_C.emb_gather`` / ``_C.emb_pooled`` launch per embedding
+  dim writes all features straight into their *group* buffers.  A group is
+  a list of features whose embeddings are concatenated along the last dim
+  (the OneTrans pool tokenizer input ``[B, L, 3E]``, the NS scalar block),
+  so the reference's ``torch.cat`` disappears and the output is produced in
+  the compute dtype (bf16) directly.
+* backward -- ``_C.emb_keys`` + a key sort + ``_C.emb_reduce_update``: the
+  gradients of all features that share a table are reduced per row and the
+  optimizer is applied once per touched row.
+
+``native=False`` (CPU, or ``PD_KERNELS=eager``) runs the same semantics in
+plain PyTorch; it is the oracle of the kernel tests.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from primus_dlrm_b200.ops import _ext
+
+OPT_KIND = {
+    "sgd": 0, "exact_sgd": 0,
+    "adagrad": 1, "exact_adagrad": 1,
+    "row_wise_adagrad": 2, "rowwise_adagrad": 2, "exact_row_wise_adagrad": 2,
+    "adam": 3, "exact_adam": 3,
+}
+
+
+@dataclass
+class SparseOptimizer:
+    """Optimizer applied to embedding rows inside the backward."""
+    kind: str = "adam"
+    lr: float = 1e-2
+    eps: float = 1e-8
+    weight_decay: float = 0.0
+    beta1: float = 0.9
+    beta2: float = 0.999
+    lr_scale: float = 1.0  # sparse warm-up multiplier (set by the trainer)
+    step: int = 0
+
+    def __post_init__(self):
+        if self.kind not in OPT_KIND:
+            raise ValueError(f"unknown embedding optimizer {self.kind!r}; "
+                             f"supported: {sorted(OPT_KIND)}")
+
+    @property
+    def code(self) -> int:
+        return OPT_KIND[self.kind]
+
+    def state_shapes(self, rows: int, dim: int) -> list[tuple[int, ...]]:
+        c = self.code
+        if c == 0:
+            return []
+        if c == 1:
+            return [(rows, dim)]
+        if c == 2:
+            return [(rows,)]
+        return [(rows, dim), (rows, dim)]
+
+    def bias_corrections(self) -> tuple[float, float]:
+        t = max(self.step, 1)
+        return 1.0 - self.beta1 ** t, 1.0 - self.beta2 ** t
+
+
+@dataclass
+class TableShard:
+    """The part of one embedding table that lives on this rank.
+
+    ``rows`` is the global row count.  Rows ``[local_row0, local_row0 +
+    local_rows)`` are stored in ``weight``.  ``peer_ptrs`` (int64 CUDA tensor,
+    one base pointer per row shard, ``chunk`` rows each) lets the gather
+    kernel read any row of the table; for an unsharded table it holds only
+    ``weight``'s pointer.
+    """
+    name: str
+    rows: int
+    dim: int
+    weight: torch.Tensor
+    state: list[torch.Tensor] = field(default_factory=list)
+    local_row0: int = 0
+    chunk: int = 0
+    n_shards: int = 1
+    peer_ptrs: torch.Tensor | None = None
+
+    def __post_init__(self):
+        if self.chunk <= 0:
+            self.chunk = self.rows
+
+    @property
+    def local_rows(self) -> int:
+        return self.weight.shape[0]
+
+    def device_ptrs(self) -> torch.Tensor:
+        if self.peer_ptrs is not None:
+            return self.peer_ptrs
+        key = (self.weight.data_ptr(), self.weight.device)
+        cached = getattr(self, "_ptr_cache", None)
+        if cached is None or cached[0] != key:
+            t = torch.tensor([self.weight.data_ptr()], dtype=torch.int64).to(self.weight.device)
+            self._ptr_cache = (key, t)
+        return self._ptr_cache[1]
+
+
+@dataclass
+class Slot:
+    """One feature of a lookup: ids -> columns [col, col+dim) of group ``group``."""
+    table: int           # index into the lookup's table list
+    group: int
+    col: int
+    pool: int = 0        # 0 none, 1 sum, 2 mean
+    pad_id: int = -1     # pooled: id excluded from bags
+    offsets: torch.Tensor | None = None  # pooled jagged bags
+
+
+@dataclass
+class LookupSpec:
+    tables: list[TableShard]
+    slots: list[Slot]
+    group_shapes: list[tuple[int, ...]]   # full output shape per group
+    dtype: torch.dtype
+    optimizer: SparseOptimizer
+    native: bool
+    err: torch.Tensor | None = None
+
+
+def _slot_view(buf: torch.Tensor, col: int, dim: int) -> torch.Tensor:
+    flat = buf.view(-1, buf.shape[-1])
+    return flat[:, col:col + dim]
+
+
+# ---------------------------------------------------------------------------
+# eager (oracle) implementations
+# ---------------------------------------------------------------------------
+
+def _eager_rows(t: TableShard, ids: torch.Tensor) -> torch.Tensor:
+    local = ids.long() - t.local_row0
+    return F.embedding(local.clamp(0, t.local_rows - 1), t.weight) * \
+        ((local >= 0) & (local < t.local_rows)).unsqueeze(-1).to(t.weight.dtype)
+
+
+def _eager_pooled(t: TableShard, ids: torch.Tensor, sl: Slot, n_bags: int) -> torch.Tensor:
+    flat = ids.reshape(-1).long()
+    if sl.offsets is not None:
+        lens = sl.offsets[1:] - sl.offsets[:-1]
+        bag = torch.repeat_interleave(torch.arange(n_bags, device=ids.device), lens)
+    else:
+        L = flat.numel() // max(n_bags, 1)
+        bag = torch.arange(flat.numel(), device=ids.device) // max(L, 1)
+    keep = flat != sl.pad_id
+    rows = _eager_rows(t, flat) * keep.unsqueeze(-1)
+    out = torch.zeros(n_bags, t.dim, dtype=t.weight.dtype, device=ids.device)
+    out.index_add_(0, bag, rows)
+    if sl.pool == 2:
+        cnt = torch.zeros(n_bags, dtype=t.weight.dtype, device=ids.device).index_add_(0, bag, keep.to(t.weight.dtype))
+        out = out / cnt.clamp_min(1).unsqueeze(-1)
+    return out
+
+
+def eager_sparse_update(t: TableShard, opt: SparseOptimizer, rows: torch.Tensor,
+                        grads: torch.Tensor) -> None:
+    """Reduce ``grads`` per row and apply ``opt`` to the touched local rows."""
+    if rows.numel() == 0:
+        return
+    local = rows.long() - t.local_row0
+    keep = (local >= 0) & (local < t.local_rows)
+    local, grads = local[keep], grads[keep].float()
+    uniq, inv = torch.unique(local, return_inverse=True)
+    g = torch.zeros(uniq.numel(), t.dim, dtype=torch.float32, device=grads.device).index_add_(0, inv, grads)
+    w = t.weight[uniq].float()
+    if opt.weight_decay:
+        g = g + opt.weight_decay * w
+    lr = opt.lr * opt.lr_scale
+    c = opt.code
+    if c == 0:
+        w = w - lr * g
+    elif c == 1:
+        s = t.state[0][uniq] + g * g
+        t.state[0][uniq] = s
+        w = w - lr * g / (s.sqrt() + opt.eps)
+    elif c == 2:
+        G = t.state[0][uniq] + (g * g).mean(dim=1)
+        t.state[0][uniq] = G
+        w = w - (lr / (G.sqrt() + opt.eps)).unsqueeze(1) * g
+    else:
+        bc1, bc2 = opt.bias_corrections()
+        m = opt.beta1 * t.state[0][uniq] + (1 - opt.beta1) * g
+        v = opt.beta2 * t.state[1][uniq] + (1 - opt.beta2) * g * g
+        t.state[0][uniq] = m
+        t.state[1][uniq] = v
+        w = w - (lr / bc1) * m / (v.sqrt() / math.sqrt(bc2) + opt.eps)
+    t.weight[uniq] = w.to(t.weight.dtype)
+
+
+# ---------------------------------------------------------------------------
+# native launch helpers
+# ---------------------------------------------------------------------------
+
+def _table_meta(tables: list[TableShard]) -> torch.Tensor:
+    rows, key = [], 0
+    for t in tables:
+        rows.append([t.rows, t.chunk, key, t.local_row0, t.n_shards, t.dim])
+        key += t.rows
+    return torch.tensor(rows, dtype=torch.int64)
+
+
+def _by_dim(spec: LookupSpec) -> dict[int, list[int]]:
+    out: dict[int, list[int]] = {}
+    for i, sl in enumerate(spec.slots):
+        out.setdefault(spec.tables[sl.table].dim, []).append(i)
+    return out
+
+
+def _launch_tables(spec: LookupSpec, slot_ids: list[int]):
+    """Tables referenced by ``slot_ids`` with a launch-local index remap."""
+    order: list[int] = []
+    for i in slot_ids:
+        ti = spec.slots[i].table
+        if ti not in order:
+            order.append(ti)
+    remap = {ti: k for k, ti in enumerate(order)}
+    return [spec.tables[ti] for ti in order], remap
+
+
+def _native_forward(spec: LookupSpec, ids: list[torch.Tensor], outs: list[torch.Tensor]) -> None:
+    C = _ext.core()
+    for dim, sidx in _by_dim(spec).items():
+        tables, remap = _launch_tables(spec, sidx)
+        weights = [t.weight for t in tables]
+        ptrs = [t.device_ptrs() for t in tables]
+        tmeta = _table_meta(tables)
+        unpooled = [i for i in sidx if spec.slots[i].pool == 0]
+        pooled = [i for i in sidx if spec.slots[i].pool != 0]
+        if unpooled:
+            meta = torch.tensor([[remap[spec.slots[i].table], 0, 0, -1] for i in unpooled], dtype=torch.int64)
+            views = [_slot_view(outs[spec.slots[i].group], spec.slots[i].col, dim) for i in unpooled]
+            C.emb_gather([ids[i] for i in unpooled], views, meta, weights, ptrs, tmeta, dim, spec.err)
+        if pooled:
+            meta, offs = [], []
+            for i in pooled:
+                sl = spec.slots[i]
+                nb = outs[sl.group].numel() // outs[sl.group].shape[-1]
+                L = ids[i].numel() // max(nb, 1) if sl.offsets is None else 0
+                meta.append([remap[sl.table], sl.pool, L, sl.pad_id])
+                offs.append(sl.offsets if sl.offsets is not None else ids[i].new_empty(0, dtype=torch.int64))
+            meta = torch.tensor(meta, dtype=torch.int64)
+            views = [_slot_view(outs[spec.slots[i].group], spec.slots[i].col, dim) for i in pooled]
+            C.emb_pooled([ids[i] for i in pooled], views, meta, offs, weights, ptrs, tmeta, dim, spec.err)
+
+
+def _native_backward(spec: LookupSpec, ids: list[torch.Tensor], grads: list[torch.Tensor]) -> None:
+    C = _ext.core()
+    opt = spec.optimizer
+    bc1, bc2 = opt.bias_corrections()
+    for dim, sidx in _by_dim(spec).items():
+        tables, remap = _launch_tables(spec, sidx)
+        weights = [t.weight for t in tables]
+        ptrs = [t.device_ptrs() for t in tables]
+        tmeta = _table_meta(tables)
+        slot_ids = [ids[i].reshape(-1) for i in sidx]
+        views, meta4, meta5, offs = [], [], [], []
+        any_pooled = False
+        for i in sidx:
+            sl = spec.slots[i]
+            views.append(_slot_view(grads[sl.group], sl.col, dim))
+            if sl.pool:
+                any_pooled = True
+                nb = grads[sl.group].numel() // grads[sl.group].shape[-1]
+                L = ids[i].numel() // max(nb, 1) if sl.offsets is None else 0
+            else:
+                L = 0
+            meta4.append([remap[sl.table], sl.pool, L, sl.pad_id])
+            meta5.append([remap[sl.table], sl.pool, L, sl.pad_id, ids[i].numel()])
+            offs.append(sl.offsets if sl.offsets is not None else ids[i].new_empty(0, dtype=torch.int64))
+        meta4 = torch.tensor(meta4, dtype=torch.int64)
+        meta5 = torch.tensor(meta5, dtype=torch.int64)
+        keys = C.emb_keys(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
+        skeys, perm = torch.sort(keys)
+        scale = grow = None
+        if any_pooled:
+            scale, grow = C.emb_pooled_scale(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
+        s1 = [t.state[0] if len(t.state) > 0 else t.weight.new_empty(0) for t in tables]
+        s2 = [t.state[1] if len(t.state) > 1 else t.weight.new_empty(0) for t in tables]
+        C.emb_reduce_update(views, meta5, weights, ptrs, s1, s2, tmeta, dim, skeys, perm, scale, grow,
+                            opt.code, opt.lr * opt.lr_scale, opt.eps, opt.weight_decay, opt.beta1,
+                            opt.beta2, bc1, bc2, spec.err)
+
+
+def _eager_backward(spec: LookupSpec, ids: list[torch.Tensor], grads: list[torch.Tensor]) -> None:
+    per_table: dict[int, tuple[list, list]] = {}
+    for i, sl in enumerate(spec.slots):
+        t = spec.tables[sl.table]
+        g = _slot_view(grads[sl.group], sl.col, t.dim).float()
+        flat = ids[i].reshape(-1).long()
+        if sl.pool:
+            nb = g.shape[0]
+            if sl.offsets is not None:
+                lens = sl.offsets[1:] - sl.offsets[:-1]
+                bag = torch.repeat_interleave(torch.arange(nb, device=flat.device), lens)
+            else:
+                bag = torch.arange(flat.numel(), device=flat.device) // max(flat.numel() // max(nb, 1), 1)
+            keep = flat != sl.pad_id
+            gr = g[bag]
+            if sl.pool == 2:
+                cnt = torch.zeros(nb, device=flat.device).index_add_(0, bag, keep.float())
+                gr = gr / cnt.clamp_min(1)[bag].unsqueeze(-1)
+            flat, gr = flat[keep], gr[keep]
+        else:
+            gr = g
+        r, gl = per_table.setdefault(sl.table, ([], []))
+        r.append(flat)
+        gl.append(gr)
+    for ti, (r, gl) in per_table.items():
+        eager_sparse_update(spec.tables[ti], spec.optimizer, torch.cat(r), torch.cat(gl))
+
+
+class GroupedLookup(torch.autograd.Function):
+    """Forward: gather all slots into their group buffers.
+    Backward: fused per-row reduction + sparse optimizer (no grads returned)."""
+
+    @staticmethod
+    def forward(ctx, anchor, spec: LookupSpec, *ids):
+        dev = spec.tables[0].weight.device
+        outs = [torch.empty(shape, dtype=spec.dtype, device=dev) for shape in spec.group_shapes]
+        if spec.native:
+            _native_forward(spec, list(ids), outs)
+        else:
+            for i, sl in enumerate(spec.slots):
+                t = spec.tables[sl.table]
+                view = _slot_view(outs[sl.group], sl.col, t.dim)
+                if sl.pool:
+                    view.copy_(_eager_pooled(t, ids[i], sl, view.shape[0]))
+                else:
+                    view.copy_(_eager_rows(t, ids[i].reshape(-1)))
+        ctx.spec = spec
+        ctx.save_for_backward(*ids)
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        spec: LookupSpec = ctx.spec
+        ids = list(ctx.saved_tensors)
+        gs = []
+        for g, shape in zip(grads, spec.group_shapes):
+            if g is None:
+                g = torch.zeros(shape, dtype=spec.dtype, device=spec.tables[0].weight.device)
+            gs.append(g.contiguous())
+        spec.optimizer.step += 1
+        with torch.no_grad():
+            if spec.native:
+                _native_backward(spec, ids, gs)
+            else:
+                _eager_backward(spec, ids, gs)
+        return (None, None) + (None,) * len(ids)
+
+
+def grouped_lookup(spec: LookupSpec, ids: list[torch.Tensor], anchor: torch.Tensor) -> list[torch.Tensor]:
+    if anchor.requires_grad and torch.is_grad_enabled():
+        return list(GroupedLookup.apply(anchor, spec, *ids))
+    with torch.no_grad():
+        return list(GroupedLookup.forward(_NoCtx(), None, spec, *ids))
+
+
+class _NoCtx:
+    def save_for_backward(self, *a):
+        pass

@@ -1,0 +1,111 @@
+"""RMSNorm / LayerNorm (optionally fused with the residual add that feeds them).
+
+Native path: ``_C.norm_fwd`` / ``_C.norm_bwd`` (one warp per row, bf16 in/out,
+fp32 statistics).  Eager path: the reference formula
+``(x.float() * rsqrt(mean(x^2) + eps)).to(x.dtype) * w``
+(``primus_dlrm/models/onetrans.py:74-82``), which is also the test oracle.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from primus_dlrm_b200.ops import _ext
+
+
+def _use_native(x: torch.Tensor) -> bool:
+    return x.is_cuda and x.dtype == torch.bfloat16 and _ext.native_enabled(x.device) \
+        and x.shape[-1] % 8 == 0 and x.shape[-1] <= 2048
+
+
+class _NormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, res, weight, bias, eps: float, kind: int):
+        C = _ext.core()
+        xc = x.contiguous()
+        rc = res.contiguous() if res is not None else None
+        y, z, rstd, mean = C.norm_fwd(xc, rc, weight, bias, eps, kind)
+        xin = z if res is not None else xc
+        ctx.kind = kind
+        ctx.fused = res is not None
+        ctx.has_bias = bias is not None
+        ctx.save_for_backward(xin, weight, rstd, mean if kind == 1 else rstd)
+        if res is not None:
+            return y, z
+        return y
+
+    @staticmethod
+    def backward(ctx, *grads):
+        C = _ext.core()
+        xin, weight, rstd, mean = ctx.saved_tensors
+        if ctx.fused:
+            dy, dz = grads
+        else:
+            (dy,), dz = grads, None
+        if dy is None:
+            dy = torch.zeros_like(xin)
+        dx, dw, db = C.norm_bwd(xin, dy.to(torch.bfloat16), dz.to(torch.bfloat16) if dz is not None else None,
+                                weight, rstd, mean if ctx.kind == 1 else None, ctx.kind)
+        return (dx, dx if ctx.fused else None, dw, db if ctx.has_bias else None, None, None)
+
+
+def rms_norm_ref(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    rms = x.float().pow(2).mean(-1, keepdim=True).add(eps).rsqrt()
+    return (x.float() * rms).to(x.dtype) * weight
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    if _use_native(x):
+        return _NormFn.apply(x, None, weight, None, eps, 0)
+    return rms_norm_ref(x, weight, eps)
+
+
+def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    if _use_native(x):
+        return _NormFn.apply(x, None, weight, bias, eps, 1)
+    return torch.nn.functional.layer_norm(x.float(), (x.shape[-1],), weight, bias, eps).to(x.dtype)
+
+
+def add_norm(a: torch.Tensor, b: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
+             eps: float, kind: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """z = a + b; returns (norm(z), z) with one pass over memory when native."""
+    if _use_native(a) and b.dtype == a.dtype and b.shape == a.shape:
+        y, z = _NormFn.apply(a, b, weight, bias, eps, kind)
+        return y, z
+    z = a + b
+    if kind == 0:
+        return rms_norm_ref(z, weight, eps), z
+    return torch.nn.functional.layer_norm(z.float(), (z.shape[-1],), weight, bias, eps).to(z.dtype), z
+
+
+class RMSNorm(nn.Module):
+    """Same parameters and state-dict key (``weight``) as the reference module."""
+
+    def __init__(self, d: int, eps: float = 1e-6):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(d))
+        self.eps = eps
+        self.kind = 0
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return rms_norm(x, self.weight, self.eps)
+
+
+class LayerNorm(nn.Module):
+    def __init__(self, d: int, eps: float = 1e-6):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(d))
+        self.bias = nn.Parameter(torch.zeros(d))
+        self.eps = eps
+        self.kind = 1
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return layer_norm(x, self.weight, self.bias, self.eps)
+
+
+def make_norm(kind: str, d: int) -> nn.Module:
+    if kind == "rmsnorm":
+        return RMSNorm(d)
+    if kind == "layernorm":
+        return LayerNorm(d)
+    raise ValueError(f"unknown norm {kind!r} (rmsnorm | layernorm)")

@@ -1,0 +1,146 @@
+"""One training step: forward (+fused heads/loss), backward (+fused sparse
+optimizer), dense-gradient sync, clip + AdamW, LR schedules.
+
+This is the step the reference runs in ``DistributedTrainer._sequential_steps``
+(``primus_dlrm/training/dist_trainer.py:460-482``) with the following changes:
+
+* dense parameters live in one flat fp32 arena; clip + AdamW are two fused
+  launches and the data-parallel gradient sync works on slices of one buffer;
+* bf16 autocast without a GradScaler (it is a no-op for bf16,
+  ``dist_trainer.py:339-345``);
+* the loss is not read back to the host inside ``step`` (the reference defers
+  ``.item()`` to log steps too, ``dist_trainer.py:611-615``).
+"""
+from __future__ import annotations
+
+import math
+import time
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+from torch.optim.lr_scheduler import CosineAnnealingLR, LinearLR, SequentialLR
+
+from primus_dlrm_b200.config import Config
+from primus_dlrm_b200.data.batch import PackedBatch
+from primus_dlrm_b200.ops.optim import FlatParams, FusedAdamW
+from primus_dlrm_b200.training.losses import InBatchBPRLoss, MultiTaskLoss
+
+
+def dense_parameters(model: nn.Module) -> list[nn.Parameter]:
+    """Trainable parameters that are not embedding tables (tables are updated
+    by the fused sparse optimizer and have requires_grad=False)."""
+    return [p for p in model.parameters() if p.requires_grad]
+
+
+class TrainEngine:
+    def __init__(self, model: nn.Module, config: Config, device: torch.device,
+                 grad_sync=None, total_steps: int | None = None, dense_optimizer=None):
+        self.model = model
+        self.config = config
+        self.device = torch.device(device)
+        tc = config.train
+        self.tasks = [k for k, v in tc.loss_weights.items() if v > 0]
+        self.flat = FlatParams(dense_parameters(model))
+        if dense_optimizer is not None:
+            self.optimizer = dense_optimizer
+        elif tc.dense_optimizer == "adamw":
+            self.optimizer = FusedAdamW(self.flat, lr=tc.lr, weight_decay=tc.weight_decay,
+                                        max_grad_norm=tc.grad_clip)
+        elif tc.dense_optimizer == "shampoo":
+            self.optimizer = _make_shampoo(self.flat.params, tc)
+        else:
+            raise ValueError(f"Unknown dense_optimizer='{tc.dense_optimizer}'. Supported: 'adamw', 'shampoo'")
+        total = total_steps if total_steps is not None else max(tc.epochs, 1) * 10_000_000
+        warm = LinearLR(self.optimizer, start_factor=tc.warmup_start_factor, total_iters=max(tc.warmup_steps, 1))
+        cos = CosineAnnealingLR(self.optimizer, T_max=max(total - tc.warmup_steps, 1))
+        self.scheduler = SequentialLR(self.optimizer, [warm, cos], milestones=[max(tc.warmup_steps, 1)])
+        self.loss_fn = MultiTaskLoss(tc.loss_weights, tc.regression_tasks)
+        self.bpr = InBatchBPRLoss(tc.contrastive_temperature) if tc.contrastive_weight > 0 else None
+        self.grad_sync = grad_sync
+        self.global_step = 0
+        self.skipped_steps = 0
+        self.use_amp = tc.bf16
+        inner = getattr(model, "module", model)
+        self.sparse_opt = inner.emb.optimizer if hasattr(inner, "emb") else None
+        self._loss_buf = torch.zeros(1, device=self.device)
+        self._host_loss = torch.zeros(1).pin_memory() if self.device.type == "cuda" else torch.zeros(1)
+        self._staging: dict[int, torch.Tensor] = {}
+
+    # ------------------------------------------------------------------
+    def _inner(self):
+        return getattr(self.model, "module", self.model)
+
+    def compute_loss(self, batch: dict[str, torch.Tensor]):
+        inner = self._inner()
+        tc = self.config.train
+        if self.bpr is not None:
+            preds, cross = inner.forward_with_cross_scores(batch, cross_task=self.tasks[0])
+            total, task_losses = self.loss_fn(preds, {t: batch[t] for t in self.tasks})
+            bpr = self.bpr(cross, batch[self.tasks[0]])
+            task_losses["bpr"] = bpr
+            return total + tc.contrastive_weight * bpr, task_losses
+        if hasattr(inner, "forward_loss") and tc.kernels == "native":
+            total, task_losses, _ = inner.forward_loss(batch, tc.loss_weights, tc.regression_tasks)
+            return total, task_losses
+        preds = self.model(batch)
+        return self.loss_fn(preds, {t: batch[t] for t in self.tasks if t in batch})
+
+    def step(self, batch: dict[str, torch.Tensor]):
+        """One optimisation step on a device-resident batch.
+        Returns (detached loss tensor, {task: loss tensor})."""
+        tc = self.config.train
+        if self.sparse_opt is not None:
+            self.sparse_opt.lr_scale = tc.sparse_warmup_value if self.global_step < tc.sparse_warmup_steps else 1.0
+        self.model.train()
+        self.flat.zero_grad()
+        with torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.use_amp):
+            total, task_losses = self.compute_loss(batch)
+        total.backward()
+        if self.grad_sync is not None:
+            self.grad_sync.sync(self.flat.grad)
+        if tc.nan_guard and not bool(torch.isfinite(total)):
+            self.skipped_steps += 1
+        else:
+            self.optimizer.step()
+        self.scheduler.step()
+        self.global_step += 1
+        return total.detach(), task_losses
+
+    def step_host(self, packed: PackedBatch) -> float:
+        """End-to-end step through the public API: pinned host batch -> H2D
+        copy -> step -> loss read back to the host."""
+        buf = self._staging.get(packed.nbytes)
+        if buf is None:
+            buf = torch.empty(packed.nbytes, dtype=torch.uint8, device=self.device)
+            self._staging[packed.nbytes] = buf
+        batch = packed.to_device(self.device, out=buf)
+        loss, _ = self.step(batch)
+        self._host_loss.copy_(loss.reshape(1), non_blocking=True)
+        if self.device.type == "cuda":
+            torch.cuda.current_stream(self.device).synchronize()
+        return float(self._host_loss[0])
+
+    def state_dict(self) -> dict:
+        return {"optimizer": self.optimizer.state_dict(), "scheduler": self.scheduler.state_dict(),
+                "global_step": self.global_step}
+
+    def load_state_dict(self, sd: dict) -> None:
+        self.optimizer.load_state_dict(sd["optimizer"])
+        self.scheduler.load_state_dict(sd["scheduler"])
+        self.global_step = int(sd.get("global_step", 0))
+
+
+def _make_shampoo(params, tc):
+    """Distributed Shampoo (optional dependency, ``dist_trainer.py:175-230``)."""
+    try:
+        from distributed_shampoo import DistributedShampoo
+        from distributed_shampoo.shampoo_types import AdaGradPreconditionerConfig
+    except ImportError as e:
+        raise RuntimeError("dense_optimizer='shampoo' needs the distributed_shampoo package "
+                           "(facebookresearch/optimizers), which is not installed") from e
+    return DistributedShampoo(params, lr=tc.lr, betas=(0.9, 1.0), epsilon=1e-4, weight_decay=tc.weight_decay,
+                              max_preconditioner_dim=tc.shampoo_max_preconditioner_dim,
+                              precondition_frequency=tc.shampoo_precondition_frequency,
+                              start_preconditioning_step=tc.shampoo_precondition_frequency,
+                              grafting_config=AdaGradPreconditionerConfig(epsilon=1.4285714285714e-05))
