@@ -462,6 +462,7 @@ static void fill_tables(GatherParams& P, const std::vector<at::Tensor>& weights,
     T.state2 = state2[t].numel() ? state2[t].data_ptr<float>() : nullptr;
     T.rows = m[t][0]; T.chunk = m[t][1]; T.key_base = m[t][2];
     T.local_row0 = m[t][3]; T.n_shards = int(m[t][4]); T.dim = int(m[t][5]);
+    T.local_rows = weights[t].size(0);
     TORCH_CHECK(T.dim == P.dim, "all tables of one launch must share the embedding dim");
     TORCH_CHECK(T.chunk > 0 && T.n_shards >= 1 && shard_ptrs[t].numel() == T.n_shards);
   }

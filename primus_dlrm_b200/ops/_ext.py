@@ -23,7 +23,9 @@ def _load(name: str):
     try:
         mod = importlib.import_module(f"primus_dlrm_b200.{name}")
     except ImportError as e:  # pragma: no cover - exercised on GPU boxes only
-        if torch.cuda.is_available():
+        src = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                           "csrc", "gemm_bindings.cpp" if name == "_gemm" else "bindings.cpp")
+        if torch.cuda.is_available() and os.path.exists(src):
             raise RuntimeError(
                 f"primus_dlrm_b200.{name} is not built; run `python setup.py build_ext --inplace` "
                 f"(sm_100a). A CUDA device is present, so no eager fallback is used.") from e
