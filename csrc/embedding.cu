@@ -686,3 +686,103 @@ void emb_reduce_update(std::vector<at::Tensor> grads, at::Tensor slot_meta,
 }
 
 }  // namespace pd
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the fused sparse update (declared in noalloc.h).
+// Same kernel as emb_reduce_update, for one table, with its scratch rows and
+// arrival counters taken from fixed file-scope device arrays instead of the
+// PyTorch allocator.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+#include "noalloc.h"
+
+namespace pd {
+namespace {
+constexpr int64_t kNaChunks = PD_NOALLOC_MAX_IDS / kChunk;
+static __device__ __align__(256) float g_na_scratch[kNaChunks * PD_NOALLOC_MAX_DIM];
+static __device__ __align__(256) int g_na_arrivals[kNaChunks];
+
+struct NaDevice {
+  bool ready = false;
+  float* scratch = nullptr;
+  int* arrivals = nullptr;
+};
+std::mutex g_na_mu;
+NaDevice g_na_dev[128];
+}  // namespace
+}  // namespace pd
+
+extern "C" int pd_emb_sparse_update_noalloc(
+    const int64_t* sorted_keys, const int64_t* perm, int64_t n, const void* grads, int grad_dtype,
+    int64_t grad_stride, float* weight, int64_t rows, int dim, float* state1, float* state2, int opt_kind,
+    float lr, float eps, float weight_decay, float beta1, float beta2, float bc1, float bc2, int* err,
+    cudaStream_t stream) {
+  using namespace pd;
+  if (n < 0 || dim <= 0) return PD_NOALLOC_BAD_ARG;
+  if (n > PD_NOALLOC_MAX_IDS || dim > PD_NOALLOC_MAX_DIM) return PD_NOALLOC_TOO_LARGE;
+  if (dim % 4 != 0 || opt_kind < 0 || opt_kind > 3 || (grad_dtype != 0 && grad_dtype != 1)) return PD_NOALLOC_BAD_ARG;
+  if (n == 0) return 0;
+  if (!sorted_keys || !perm || !grads || !weight || rows <= 0) return PD_NOALLOC_BAD_ARG;
+  if ((opt_kind == 1 || opt_kind == 2) && !state1) return PD_NOALLOC_BAD_ARG;
+  if (opt_kind == 3 && (!state1 || !state2)) return PD_NOALLOC_BAD_ARG;
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return int(e);
+  if (dev < 0 || dev >= 128) return PD_NOALLOC_BAD_ARG;
+  NaDevice* nd = &g_na_dev[dev];
+  {
+    std::lock_guard<std::mutex> lock(g_na_mu);
+    if (!nd->ready) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_na_scratch);
+      if (e != cudaSuccess) return int(e);
+      nd->scratch = static_cast<float*>(p);
+      e = cudaGetSymbolAddress(&p, g_na_arrivals);
+      if (e != cudaSuccess) return int(e);
+      nd->arrivals = static_cast<int*>(p);
+      nd->ready = true;
+    }
+  }
+  const int64_t n_chunks = (n + kChunk - 1) / kChunk;
+  e = cudaMemsetAsync(nd->scratch, 0, size_t(n_chunks) * dim * sizeof(float), stream);
+  if (e != cudaSuccess) return int(e);
+  e = cudaMemsetAsync(nd->arrivals, 0, size_t(n_chunks) * sizeof(int), stream);
+  if (e != cudaSuccess) return int(e);
+
+  GatherParams P;
+  memset(&P, 0, sizeof(P));
+  P.dim = dim;
+  P.n_slots = 1;
+  P.slots[0].io = const_cast<void*>(grads);
+  P.slots[0].io_stride = grad_stride;
+  P.slots[0].n = n;
+  P.slot_off[0] = 0;
+  P.slot_off[1] = n;
+  P.n_tables = 1;
+  Table& T = P.tables[0];
+  T.local = weight;
+  T.state1 = state1;
+  T.state2 = state2;
+  T.rows = rows;
+  T.chunk = rows;
+  T.local_rows = rows;
+  T.n_shards = 1;
+  T.dim = dim;
+  OptParams O{opt_kind, lr, eps, weight_decay, beta1, beta2, bc1, bc2};
+  GradSrc src{perm, nullptr, nullptr};
+  int64_t blocks = (n_chunks + 7) / 8;
+  const int64_t cap = int64_t(num_sms()) * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  if (grad_dtype == 1)
+    reduce_update_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(P, O, sorted_keys, src, n, nd->scratch,
+                                                                    nd->arrivals, err);
+  else
+    reduce_update_kernel<float><<<blocks, 256, 0, stream>>>(P, O, sorted_keys, src, n, nd->scratch, nd->arrivals,
+                                                            err);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) note_launch();
+  return int(e);
+}
