@@ -36,15 +36,16 @@ __global__ void __launch_bounds__(256) norm_fwd_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ res,
     const float* __restrict__ w, const float* __restrict__ b, __nv_bfloat16* __restrict__ y,
     __nv_bfloat16* __restrict__ z, float* __restrict__ stat_rstd, float* __restrict__ stat_mean,
-    int64_t rows, int D, float eps) {
+    int64_t rows, int D, float eps, int64_t rpb, int64_t x_bstride, int64_t r_bstride) {
   const int lane = threadIdx.x & 31;
   const int nvec = D >> 3;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nw = (int64_t(gridDim.x) * blockDim.x) >> 5;
   for (int64_t r = warp; r < rows; r += nw) {
     float v[NV][8];
-    const Vec8* xr = reinterpret_cast<const Vec8*>(x + r * D);
-    const Vec8* rr = res ? reinterpret_cast<const Vec8*>(res + r * D) : nullptr;
+    const int64_t bb = r / rpb, ii = r - bb * rpb;
+    const Vec8* xr = reinterpret_cast<const Vec8*>(x + bb * x_bstride + ii * D);
+    const Vec8* rr = res ? reinterpret_cast<const Vec8*>(res + bb * r_bstride + ii * D) : nullptr;
     float s = 0.f;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
@@ -182,32 +183,49 @@ static void check_rows(const at::Tensor& t, int64_t D) {
   TORCH_CHECK(t.size(-1) == D);
 }
 
+// [B, R, D] view whose rows are contiguous within a batch (any batch stride).
+static void check_batch_rows(const at::Tensor& t, int64_t D) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, "norm inputs must be bf16 CUDA tensors");
+  TORCH_CHECK(t.dim() == 3 && t.size(2) == D && t.stride(2) == 1 && (t.size(1) == 1 || t.stride(1) == D),
+              "norm input must be [B, R, D] with contiguous rows");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0 && t.stride(0) % 8 == 0,
+              "norm input rows must be 16-byte aligned");
+}
+
 // Returns {y, z_or_empty, rstd, mean_or_empty}
 std::vector<at::Tensor> norm_fwd(at::Tensor x, c10::optional<at::Tensor> res, at::Tensor w,
                                  c10::optional<at::Tensor> b, double eps, int64_t kind) {
   const int64_t D = x.size(-1);
   TORCH_CHECK(D % 8 == 0 && D <= 256 * kNormMaxVec, "norm dim must be a multiple of 8 and <= 2048");
-  check_rows(x, D);
-  if (res) check_rows(*res, D);
+  at::Tensor x3 = x.dim() == 3 ? x : x.reshape({1, -1, D});
+  check_batch_rows(x3, D);
+  at::Tensor r3;
+  if (res) {
+    r3 = res->dim() == 3 ? *res : res->reshape({1, -1, D});
+    check_batch_rows(r3, D);
+    TORCH_CHECK(r3.size(0) == x3.size(0) && r3.size(1) == x3.size(1));
+  }
   TORCH_CHECK(w.scalar_type() == at::kFloat && w.numel() == D);
-  const int64_t rows = x.numel() / D;
-  auto y = at::empty_like(x);
-  at::Tensor z = res ? at::empty_like(x) : at::Tensor();
+  const int64_t rows = x3.size(0) * x3.size(1);
+  const int64_t rpb = x3.size(1) > 0 ? x3.size(1) : 1;
+  auto y = at::empty(x.sizes(), x.options());
+  at::Tensor z = res ? at::empty(x.sizes(), x.options()) : at::Tensor();
   auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
   at::Tensor mean = kind == 1 ? at::empty({rows}, x.options().dtype(at::kFloat)) : at::Tensor();
   if (rows == 0) return {y, z, rstd, mean};
   int64_t blocks = (rows + 7) / 8;
   const int64_t cap = int64_t(num_sms()) * 8;
   if (blocks > cap) blocks = cap;
-  auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
-  auto rp = res ? reinterpret_cast<const __nv_bfloat16*>(res->data_ptr()) : nullptr;
+  auto xp = reinterpret_cast<const __nv_bfloat16*>(x3.data_ptr());
+  auto rp = res ? reinterpret_cast<const __nv_bfloat16*>(r3.data_ptr()) : nullptr;
+  const int64_t xbs = x3.stride(0), rbs = res ? r3.stride(0) : 0;
   auto yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
   auto zp = res ? reinterpret_cast<__nv_bfloat16*>(z.data_ptr()) : nullptr;
   const float* bp = kind == 1 ? b->data_ptr<float>() : nullptr;
   float* mp = kind == 1 ? mean.data_ptr<float>() : nullptr;
   const int nv = int((D / 8 + 31) / 32);
 #define PD_NF(K, NVv) norm_fwd_kernel<K, NVv><<<blocks, 256, 0, stream()>>>(xp, rp, w.data_ptr<float>(), bp, yp, zp, \
-                                                   rstd.data_ptr<float>(), mp, rows, int(D), float(eps))
+                                                   rstd.data_ptr<float>(), mp, rows, int(D), float(eps), rpb, xbs, rbs)
 #define PD_NF_K(K) if (nv <= 1) PD_NF(K, 1); else if (nv <= 2) PD_NF(K, 2); else if (nv <= 4) PD_NF(K, 4); else PD_NF(K, 8)
   if (kind == 0) { PD_NF_K(0); } else { PD_NF_K(1); }
 #undef PD_NF_K

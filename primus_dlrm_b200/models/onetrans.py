@@ -32,7 +32,7 @@ from primus_dlrm_b200.models.base import BaseModel
 from primus_dlrm_b200.models.embedding import Embeddings
 from primus_dlrm_b200.models.heads import fused_heads_loss
 from primus_dlrm_b200.ops import dense
-from primus_dlrm_b200.ops.attention import pyramid_attention
+from primus_dlrm_b200.ops.attention import causal_attention_all_rows, pyramid_attention
 from primus_dlrm_b200.ops.embedding import SparseOptimizer
 from primus_dlrm_b200.ops.norm import add_norm, make_norm
 
@@ -74,10 +74,16 @@ class MixedAttention(nn.Module):
         _xavier_per_token(self.ns_qkv_weight)
 
     def forward(self, x: torch.Tensor, n_s: int, q_len: int) -> torch.Tensor:
-        """x [B, T, D] (normed) -> attention output [B, q_len, D] (pre out-proj residual)."""
+        """x [B, T, D] (normed) -> out-projected attention of the last q_len
+        queries, [B, q_len, D].  On CUDA (no dropout, native impls) all T rows
+        are computed and the result is a [B, q_len, D] view of [B, T, D]."""
         B, T, D = x.shape
         qkv = dense.mixed_linear(x, n_s, self.s_qkv.weight, self.ns_qkv_weight)  # [B, T, 3D]
         qkv = qkv.view(B, T, 3, self.n_heads, self.d_head)
+        if x.is_cuda and self.attention_impl in ("fav4", "fav2", "turbo", "native") and \
+                not (self.training and self.attn_drop > 0 and self.attention_impl != "fav4"):
+            o = causal_attention_all_rows(qkv, self.n_heads).reshape(B, T, D)
+            return self.out_proj(o)[:, T - q_len:]
         q = qkv[:, T - q_len:, 0]
         k = qkv[:, :, 1]
         v = qkv[:, :, 2]
@@ -126,7 +132,7 @@ class OneTransBlock(nn.Module):
         n_ns = kv_len - n_s_tokens
         a = self.attn(self.norm1(x), n_s=n_s_tokens, q_len=q_len)
         x_tail = x[:, kv_len - q_len:]
-        y, z = add_norm(a, x_tail.contiguous() if a.is_cuda else x_tail, self.norm2.weight,
+        y, z = add_norm(a, x_tail, self.norm2.weight,
                         getattr(self.norm2, "bias", None), self.norm2.eps, self.norm2.kind)
         f = self.ffn(y, n_s=q_len - n_ns)
         return z + f

@@ -52,6 +52,20 @@ class _NativeFMHA(torch.autograd.Function):
         return dq, dk, dv, None
 
 
+def causal_attention_all_rows(qkv: torch.Tensor, n_heads: int) -> torch.Tensor:
+    """Causal attention of every row of ``qkv`` [B, T, 3, H, d] -> [B, T, H, d].
+
+    The pyramid keeps the LAST q_len queries, and the first kv_len - q_len rows
+    of a causal score matrix are also its cheapest ones, so computing all rows
+    (standard causal, q_len == kv_len) costs (kv-q)(kv-q+1)/2 extra pairs per
+    head (~2% for the v6 pyramid) and runs every layer on the fast square
+    causal kernels.  The caller keeps the last q_len rows.
+    """
+    q, k, v = qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2), qkv[:, :, 2].transpose(1, 2)
+    out = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+    return out.transpose(1, 2)
+
+
 def pyramid_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, impl: str = "auto",
                       dropout_p: float = 0.0) -> torch.Tensor:
     """q [B, q_len, H, d]; k, v [B, kv_len, H, d] -> [B, q_len, H, d]."""

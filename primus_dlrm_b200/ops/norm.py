@@ -13,6 +13,12 @@ import torch.nn as nn
 from primus_dlrm_b200.ops import _ext
 
 
+def _rows_ok(t: torch.Tensor) -> bool:
+    """[B, R, D] view with contiguous, 16-byte aligned rows (any batch stride)."""
+    return (t.dim() == 3 and t.stride(2) == 1 and (t.shape[1] == 1 or t.stride(1) == t.shape[2])
+            and t.data_ptr() % 16 == 0 and t.stride(0) % 8 == 0) or t.is_contiguous()
+
+
 def _use_native(x: torch.Tensor) -> bool:
     return x.is_cuda and x.dtype == torch.bfloat16 and _ext.native_enabled(x.device) \
         and x.shape[-1] % 8 == 0 and x.shape[-1] <= 2048
@@ -22,10 +28,12 @@ class _NormFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, res, weight, bias, eps: float, kind: int):
         C = _ext.core()
-        xc = x.contiguous()
-        rc = res.contiguous() if res is not None else None
+        xc = x if _rows_ok(x) else x.contiguous()
+        rc = (res if _rows_ok(res) else res.contiguous()) if res is not None else None
         y, z, rstd, mean = C.norm_fwd(xc, rc, weight, bias, eps, kind)
         xin = z if res is not None else xc
+        if res is None and not xin.is_contiguous():
+            xin = xin.contiguous()
         ctx.kind = kind
         ctx.fused = res is not None
         ctx.has_bias = bias is not None
@@ -69,7 +77,7 @@ def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: f
 def add_norm(a: torch.Tensor, b: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
              eps: float, kind: int) -> tuple[torch.Tensor, torch.Tensor]:
     """z = a + b; returns (norm(z), z) with one pass over memory when native."""
-    if _use_native(a) and b.dtype == a.dtype and b.shape == a.shape:
+    if _use_native(a) and b.dtype == a.dtype and b.shape == a.shape and a.dim() == 3:
         y, z = _NormFn.apply(a, b, weight, bias, eps, kind)
         return y, z
     z = a + b
