@@ -15,7 +15,8 @@ std::vector<at::Tensor> emb_pooled_scale(std::vector<at::Tensor>, std::vector<at
 void emb_reduce_update(std::vector<at::Tensor>, at::Tensor, std::vector<at::Tensor>, std::vector<at::Tensor>,
                        std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, int64_t, at::Tensor,
                        at::Tensor, c10::optional<at::Tensor>, c10::optional<at::Tensor>, int64_t, double,
-                       double, double, double, double, double, double, at::Tensor);
+                       double, double, double, double, double, double, at::Tensor, c10::optional<at::Tensor>,
+                       c10::optional<at::Tensor>);
 // norm.cu
 std::vector<at::Tensor> norm_fwd(at::Tensor, c10::optional<at::Tensor>, at::Tensor, c10::optional<at::Tensor>,
                                  double, int64_t);
@@ -31,6 +32,14 @@ void adamw_step(at::Tensor, at::Tensor, at::Tensor, at::Tensor, double, double, 
                 double, double, c10::optional<at::Tensor>);
 void scale_(at::Tensor, double);
 long long launches();
+// comm.cu
+at::Tensor alloc_shared(int64_t, int64_t);
+at::Tensor ipc_handle(at::Tensor);
+std::vector<int64_t> ipc_open(at::Tensor);
+void ipc_close(int64_t);
+void push_rows(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor);
+void signal_barrier(at::Tensor, int64_t, int64_t, int64_t, at::Tensor);
+at::Tensor owner_keys(at::Tensor, at::Tensor, int64_t);
 }  // namespace pd
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -39,7 +48,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("emb_pooled", &pd::emb_pooled);
   m.def("emb_keys", &pd::emb_keys);
   m.def("emb_pooled_scale", &pd::emb_pooled_scale);
-  m.def("emb_reduce_update", &pd::emb_reduce_update);
+  m.def("emb_reduce_update", &pd::emb_reduce_update, py::arg("grads"), py::arg("slot_meta"), py::arg("weights"),
+        py::arg("shard_ptrs"), py::arg("state1"), py::arg("state2"), py::arg("table_meta"), py::arg("dim"),
+        py::arg("sorted_keys"), py::arg("perm"), py::arg("scale"), py::arg("grad_row"), py::arg("opt_kind"),
+        py::arg("lr"), py::arg("eps"), py::arg("weight_decay"), py::arg("beta1"), py::arg("beta2"),
+        py::arg("bc1"), py::arg("bc2"), py::arg("err"), py::arg("out_rows") = py::none(),
+        py::arg("seg") = py::none());
   m.def("norm_fwd", &pd::norm_fwd);
   m.def("norm_bwd", &pd::norm_bwd);
   m.def("heads_loss_fwd", &pd::heads_loss_fwd);
@@ -47,5 +61,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grad_sqnorm", &pd::grad_sqnorm);
   m.def("adamw_step", &pd::adamw_step);
   m.def("scale_", &pd::scale_);
+  m.def("alloc_shared", &pd::alloc_shared);
+  m.def("ipc_handle", &pd::ipc_handle);
+  m.def("ipc_open", &pd::ipc_open);
+  m.def("ipc_close", &pd::ipc_close);
+  m.def("push_rows", &pd::push_rows);
+  m.def("signal_barrier", &pd::signal_barrier);
+  m.def("owner_keys", &pd::owner_keys);
   m.def("launch_count", &pd::launches, "kernels launched by this extension so far");
 }

@@ -12,6 +12,7 @@
 #include <ATen/ops/empty_like.h>
 #include <ATen/ops/zeros.h>
 #include <ATen/ops/zeros_like.h>
+#include <ATen/ops/from_blob.h>
 #include <c10/cuda/CUDAStream.h>
 #include <c10/util/Exception.h>
 #include <atomic>

@@ -246,7 +246,22 @@ struct GradSrc {
   const int64_t* perm;      // sorted q -> original position p
   const float* scale;       // per original position (pooled); nullptr = 1
   const int64_t* grad_row;  // per original position: row within the slot's grad view; nullptr = i
+  // Reduce-only mode: when out_rows != nullptr the summed gradient of the run
+  // starting at sorted position q is stored to out_rows[seg[q]] (fp32 [U, dim])
+  // instead of being applied to the table.
+  float* out_rows;
+  const int64_t* seg;
 };
+
+__device__ __forceinline__ void store_reduced(const GradSrc& src, int64_t q, const float4* acc, int nvec,
+                                              int dim, int lane) {
+  float4* o = reinterpret_cast<float4*>(src.out_rows + src.seg[q] * int64_t(dim));
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int v = lane + 32 * k;
+    if (v < nvec) o[v] = acc[k];
+  }
+}
 
 template <typename GradT>
 __device__ __forceinline__ void accum_row(float4* acc, const GradT* src, int nvec, int lane, float sc) {
@@ -388,7 +403,8 @@ __global__ void __launch_bounds__(256) reduce_update_kernel(
       const bool head = (a > 0) ? (skeys[a - 1] != key) : true;
       const bool tail = (b < total) ? (skeys[b] != key) : true;
       if (head && tail) {
-        apply_update(P, O, key, acc, nvec, lane, err);
+        if (src.out_rows) store_reduced(src, a, acc, nvec, P.dim, lane);
+        else apply_update(P, O, key, acc, nvec, lane, err);
       } else {
         // The run spans several chunks: accumulate into the head chunk's
         // scratch row; the last arriving chunk applies the update.
@@ -421,7 +437,8 @@ __global__ void __launch_bounds__(256) reduce_update_kernel(
             }
           }
           if (lane == 0) arrivals[hc] = 0;
-          apply_update(P, O, key, acc, nvec, lane, err);
+          if (src.out_rows) store_reduced(src, beg, acc, nvec, P.dim, lane);
+          else apply_update(P, O, key, acc, nvec, lane, err);
         }
       }
       a = b;
@@ -634,7 +651,8 @@ void emb_reduce_update(std::vector<at::Tensor> grads, at::Tensor slot_meta,
                        at::Tensor table_meta, int64_t dim, at::Tensor sorted_keys, at::Tensor perm,
                        c10::optional<at::Tensor> scale, c10::optional<at::Tensor> grad_row,
                        int64_t opt_kind, double lr, double eps, double weight_decay, double beta1,
-                       double beta2, double bc1, double bc2, at::Tensor err) {
+                       double beta2, double bc1, double bc2, at::Tensor err,
+                       c10::optional<at::Tensor> out_rows, c10::optional<at::Tensor> seg) {
   GatherParams P;
   P.dim = int(dim);
   fill_tables(P, weights, shard_ptrs, state1, state2, table_meta);
@@ -665,7 +683,14 @@ void emb_reduce_update(std::vector<at::Tensor> grads, at::Tensor slot_meta,
   OptParams O{int(opt_kind), float(lr), float(eps), float(weight_decay), float(beta1), float(beta2),
               float(bc1), float(bc2)};
   GradSrc src{perm.data_ptr<int64_t>(), scale ? scale->data_ptr<float>() : nullptr,
-              grad_row ? grad_row->data_ptr<int64_t>() : nullptr};
+              grad_row ? grad_row->data_ptr<int64_t>() : nullptr, nullptr, nullptr};
+  if (out_rows && out_rows->defined() && out_rows->numel() > 0) {
+    TORCH_CHECK(seg && seg->numel() == total && out_rows->scalar_type() == at::kFloat &&
+                out_rows->is_contiguous() && out_rows->size(-1) == dim,
+                "reduce-only mode needs fp32 out_rows [U, dim] and seg [N]");
+    src.out_rows = out_rows->data_ptr<float>();
+    src.seg = seg->data_ptr<int64_t>();
+  }
   const int64_t n_chunks = (total + kChunk - 1) / kChunk;
   const int dev = weights[0].get_device();
   ScratchCache& sc = scratch_for(dev);
@@ -771,7 +796,7 @@ extern "C" int pd_emb_sparse_update_noalloc(
   T.n_shards = 1;
   T.dim = dim;
   OptParams O{opt_kind, lr, eps, weight_decay, beta1, beta2, bc1, bc2};
-  GradSrc src{perm, nullptr, nullptr};
+  GradSrc src{perm, nullptr, nullptr, nullptr, nullptr};
   int64_t blocks = (n_chunks + 7) / 8;
   const int64_t cap = int64_t(num_sms()) * 16;
   if (blocks > cap) blocks = cap;

@@ -56,15 +56,26 @@ class Table(nn.Module):
         self.weight = nn.Parameter(w, requires_grad=False)
         self.shard = TableShard(name=cfg.name, rows=cfg.num_embeddings, dim=cfg.embedding_dim,
                                 weight=self.weight.data, local_row0=local_row0)
+        self.col_shards: list[TableShard] | None = None  # column-wise sharding: one shard per rank
         self.opt_state: list[torch.Tensor] = []
 
+    def lookup_shards(self) -> list[tuple[TableShard, int]]:
+        """(shard, column offset) pairs that make up one feature's embedding."""
+        if self.col_shards:
+            return [(s, c * s.dim) for c, s in enumerate(self.col_shards)]
+        return [(self.shard, 0)]
+
     def ensure_state(self, opt: SparseOptimizer) -> None:
-        shapes = opt.state_shapes(self.weight.shape[0], self.embedding_dim)
+        """Optimizer state for the locally stored rows (allocated on first use)."""
+        if self.weight.device.type == "meta":
+            return
+        shapes = opt.state_shapes(self.weight.shape[0], self.weight.shape[1])
         if len(self.opt_state) != len(shapes) or any(
                 s.device != self.weight.device or tuple(s.shape) != sh for s, sh in zip(self.opt_state, shapes)):
             self.opt_state = [torch.zeros(sh, dtype=torch.float32, device=self.weight.device) for sh in shapes]
-        self.shard.weight = self.weight.data
-        self.shard.state = self.opt_state
+        local = self.shard
+        local.weight = self.weight.data
+        local.state = self.opt_state
 
     def _apply(self, fn, recurse=True):
         out = super()._apply(fn, recurse)
@@ -118,6 +129,8 @@ class Embeddings(nn.Module):
         self._anchor: torch.Tensor | None = None
         self.err = None
         self.native = True  # set False to force the eager oracle path
+        self.executor = None  # set by parallel.sharded_embedding.shard_embeddings
+        self.sharded = False
 
     # -- bookkeeping -------------------------------------------------------
     def tables(self) -> list[Table]:
@@ -173,9 +186,6 @@ class Embeddings(nn.Module):
             for f in group:
                 t = self._feature_table[f]
                 t.ensure_state(self.optimizer)
-                if id(t) not in tindex:
-                    tindex[id(t)] = len(tables)
-                    tables.append(t.shard)
                 x = features[f]
                 device = x.device
                 pool = _POOL.get(t.pooling, 0)
@@ -188,20 +198,26 @@ class Embeddings(nn.Module):
                     lead = this_lead
                 elif lead != this_lead:
                     raise ValueError(f"group {group}: feature {f} has leading shape {this_lead}, expected {lead}")
-                slots.append(Slot(table=tindex[id(t)], group=gi, col=col, pool=pool,
-                                  pad_id=self.padding_idx if pool else -1, offsets=off))
-                ids.append(x if x.is_contiguous() else x.contiguous())
+                for shard, coff in t.lookup_shards():
+                    if id(shard) not in tindex:
+                        tindex[id(shard)] = len(tables)
+                        tables.append(shard)
+                    slots.append(Slot(table=tindex[id(shard)], group=gi, col=col + coff, pool=pool,
+                                      pad_id=self.padding_idx if pool else -1, offsets=off))
+                    ids.append(x if x.is_contiguous() else x.contiguous())
                 col += t.embedding_dim
             shapes.append(tuple(lead) + (col,))
         native = (self.native and device is not None and device.type == "cuda"
                   and _ext.native_enabled(device))
+        executor = self.executor
         if native:
             ids = [i if i.dtype in (torch.int32, torch.int64) else i.long() for i in ids]
             if len({i.dtype for i in ids}) > 1:
                 ids = [i.long() for i in ids]
         spec = LookupSpec(tables=tables, slots=slots, group_shapes=shapes, dtype=dtype,
                           optimizer=self.optimizer, native=native,
-                          err=self.error_word(device) if native else None)
+                          err=self.error_word(device) if (native or executor is not None) else None,
+                          executor=executor)
         return grouped_lookup(spec, ids, self._grad_anchor(device))
 
     def forward(self, features: dict[str, torch.Tensor], padding_idx: int = 0) -> dict[str, torch.Tensor]:

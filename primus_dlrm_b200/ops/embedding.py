@@ -94,6 +94,8 @@ class TableShard:
     chunk: int = 0
     n_shards: int = 1
     peer_ptrs: torch.Tensor | None = None
+    kind: str = "local"          # local | row_wise | table_wise | column_wise | data_parallel
+    owner: int | None = None     # owning rank of a table-wise table / column block
 
     def __post_init__(self):
         if self.chunk <= 0:
@@ -134,6 +136,7 @@ class LookupSpec:
     optimizer: SparseOptimizer
     native: bool
     err: torch.Tensor | None = None
+    executor: object | None = None   # cross-rank exchange (parallel.sharded_embedding)
 
 
 def _slot_view(buf: torch.Tensor, col: int, dim: int) -> torch.Tensor:
@@ -146,6 +149,8 @@ def _slot_view(buf: torch.Tensor, col: int, dim: int) -> torch.Tensor:
 # ---------------------------------------------------------------------------
 
 def _eager_rows(t: TableShard, ids: torch.Tensor) -> torch.Tensor:
+    if t.local_rows == 0:
+        return torch.zeros(ids.shape + (t.dim,), dtype=t.weight.dtype, device=ids.device)
     local = ids.long() - t.local_row0
     return F.embedding(local.clamp(0, t.local_rows - 1), t.weight) * \
         ((local >= 0) & (local < t.local_rows)).unsqueeze(-1).to(t.weight.dtype)
@@ -332,9 +337,11 @@ class GroupedLookup(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, anchor, spec: LookupSpec, *ids):
-        dev = spec.tables[0].weight.device
+        dev = spec.err.device if spec.err is not None else spec.tables[0].weight.device
         outs = [torch.empty(shape, dtype=spec.dtype, device=dev) for shape in spec.group_shapes]
-        if spec.native:
+        if spec.executor is not None:
+            spec.executor.forward(spec, list(ids), outs)
+        elif spec.native:
             _native_forward(spec, list(ids), outs)
         else:
             for i, sl in enumerate(spec.slots):
@@ -359,7 +366,9 @@ class GroupedLookup(torch.autograd.Function):
             gs.append(g.contiguous())
         spec.optimizer.step += 1
         with torch.no_grad():
-            if spec.native:
+            if spec.executor is not None:
+                spec.executor.backward(spec, ids, gs)
+            elif spec.native:
                 _native_backward(spec, ids, gs)
             else:
                 _eager_backward(spec, ids, gs)

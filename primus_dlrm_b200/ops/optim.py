@@ -87,30 +87,39 @@ class FusedAdamW(torch.optim.Optimizer):
         return self.flat.grad.norm()
 
     @torch.no_grad()
-    def step(self, closure=None):
+    def step(self, closure=None, shard: tuple[int, int] | None = None, group=None):
+        """Update all parameters, or only the flat slice ``shard = (a, b)``
+        (ZeRO-style sharded optimizer: the global gradient norm for clipping
+        is then all-reduced over ``group``)."""
         g = self.param_groups[0]
         lr, (b1, b2), eps, wd = g["lr"], g["betas"], g["eps"], g["weight_decay"]
         self.step_count += 1
         bc1 = 1 - b1 ** self.step_count
         bc2 = 1 - b2 ** self.step_count
         f = self.flat
-        if self.native:
-            if self.max_grad_norm > 0:
+        a, b = shard if shard is not None else (0, f.numel)
+        p, gr, m, v = f.data[a:b], f.grad[a:b], self.exp_avg[a:b], self.exp_avg_sq[a:b]
+        if self.max_grad_norm > 0:
+            if self.native:
                 self._sqnorm.zero_()
-                _ext.core().grad_sqnorm(f.grad, self._sqnorm)
-            _ext.core().adamw_step(f.data, f.grad, self.exp_avg, self.exp_avg_sq, lr, b1, b2, eps, wd,
-                                   bc1, bc2, self.max_grad_norm,
+                _ext.core().grad_sqnorm(gr, self._sqnorm)
+            else:
+                self._sqnorm.copy_(gr.float().pow(2).sum().reshape(1))
+            if shard is not None:
+                torch.distributed.all_reduce(self._sqnorm, group=group)
+        if self.native:
+            _ext.core().adamw_step(p, gr, m, v, lr, b1, b2, eps, wd, bc1, bc2, self.max_grad_norm,
                                    self._sqnorm if self.max_grad_norm > 0 else None)
             return None
-        grad = f.grad
+        grad = gr
         if self.max_grad_norm > 0:
-            coef = torch.clamp(self.max_grad_norm / (grad.norm() + 1e-6), max=1.0)
+            coef = torch.clamp(self.max_grad_norm / (self._sqnorm.sqrt() + 1e-6), max=1.0)
             grad = grad * coef
-        f.data.mul_(1 - lr * wd)
-        self.exp_avg.mul_(b1).add_(grad, alpha=1 - b1)
-        self.exp_avg_sq.mul_(b2).addcmul_(grad, grad, value=1 - b2)
-        denom = (self.exp_avg_sq.sqrt() / math.sqrt(bc2)).add_(eps)
-        f.data.addcdiv_(self.exp_avg, denom, value=-lr / bc1)
+        p.mul_(1 - lr * wd)
+        m.mul_(b1).add_(grad, alpha=1 - b1)
+        v.mul_(b2).addcmul_(grad, grad, value=1 - b2)
+        denom = (v.sqrt() / math.sqrt(bc2)).add_(eps)
+        p.addcdiv_(m, denom, value=-lr / bc1)
         return None
 
     def state_dict(self):

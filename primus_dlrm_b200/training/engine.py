@@ -101,6 +101,9 @@ class TrainEngine:
             self.grad_sync.sync(self.flat.grad)
         if tc.nan_guard and not bool(torch.isfinite(total)):
             self.skipped_steps += 1
+        elif getattr(self.grad_sync, "sharded", False) and isinstance(self.optimizer, FusedAdamW):
+            self.optimizer.step(shard=self.grad_sync.shard_range(self.flat.numel), group=self.grad_sync.group)
+            self.grad_sync.gather_params(self.flat.data)
         else:
             self.optimizer.step()
         self.scheduler.step()
@@ -120,6 +123,12 @@ class TrainEngine:
         if self.device.type == "cuda":
             torch.cuda.current_stream(self.device).synchronize()
         return float(self._host_loss[0])
+
+    def exposed_comm_ms(self) -> float:
+        """Device time of the embedding lookup + exchange since the last call."""
+        inner = self._inner()
+        ex = getattr(getattr(inner, "emb", None), "executor", None)
+        return ex.take_comm_ms() if ex is not None and hasattr(ex, "take_comm_ms") else 0.0
 
     def state_dict(self) -> dict:
         return {"optimizer": self.optimizer.state_dict(), "scheduler": self.scheduler.state_dict(),

@@ -1,0 +1,146 @@
+"""Multi-GPU (2 ranks, NCCL): the NVLink peer-memory sparse exchange against
+the collective baseline, and a short OneTrans training run through the full
+sharded stack.  Needs 2+ CUDA devices."""
+import os
+
+import pytest
+import torch
+
+from dist_utils import free_port
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+TINY = os.path.join(ROOT, "configs", "onetrans_tiny.yaml")
+
+
+def _nccl_entry(rank, world, port, fn, q):
+    import datetime
+    import traceback
+
+    import torch.distributed as dist
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "RANK": str(rank),
+                       "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank), "NCCL_NVLS_ENABLE": "0"})
+    try:
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", rank))
+        out = fn(rank, world)
+        import io
+        buf = io.BytesIO()
+        torch.save(out, buf)
+        q.put((rank, "ok", buf.getvalue()))
+    except BaseException:
+        q.put((rank, "err", traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def run_nccl(fn, world=2):
+    import io
+
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_nccl_entry, args=(r, world, port, fn, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res, errs = {}, []
+    for _ in range(world):
+        r, st, v = q.get(timeout=600)
+        if st == "ok":
+            res[r] = torch.load(io.BytesIO(v), weights_only=False)
+        else:
+            errs.append(v)
+    for p in ps:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    if errs:
+        raise RuntimeError("\n".join(errs))
+    return res
+
+
+def _cfg(comm, opt="sgd"):
+    from primus_dlrm_b200.config import Config, TableShardingSpec
+    cfg = Config.load(TINY)
+    kinds = {"item": "row_wise", "artist": "table_wise", "album": "column_wise", "uid": "data_parallel"}
+    for t in cfg.model.embedding_tables:
+        t.sharding = TableShardingSpec(sharding_type=kinds[t.name], ranks=[1] if t.name == "artist" else None)
+    cfg.distributed.embedding_sharding.enabled = True
+    cfg.distributed.comm = comm
+    cfg.train.embedding_optimizer = opt
+    cfg.train.bf16 = False
+    cfg.train.warmup_steps = 1
+    return cfg
+
+
+def _peer_vs_nccl(rank, world):
+    import copy
+
+    import torch.distributed as dist
+
+    from primus_dlrm_b200.data.synthetic import generate_batch
+    from primus_dlrm_b200.parallel.build import build_model
+    from primus_dlrm_b200.parallel.state import full_state_dict, load_full_state_dict
+    from primus_dlrm_b200.parallel.wrapper import wrap_model
+    from primus_dlrm_b200.training.engine import TrainEngine
+    dev = torch.device("cuda", rank)
+    out = {}
+    torch.manual_seed(0)
+    init = copy.deepcopy(build_model(_cfg("nccl")).state_dict())
+    for comm in ("peer", "nccl"):
+        cfg = _cfg(comm)
+        model = build_model(cfg, device=dev, meta_device=True)
+        model, sync = wrap_model(model, dev, cfg)
+        load_full_state_dict(model, init)
+        eng = TrainEngine(model, cfg, dev, grad_sync=sync)
+        losses = []
+        for s in range(3):
+            b = generate_batch(cfg, 32, seed=1000 * s + rank)
+            loss, _ = eng.step({k: v.to(dev) for k, v in b.items()})
+            losses.append(float(loss))
+        ex = model.emb.executor
+        if hasattr(ex, "check"):
+            ex.check()
+        model.emb.check_errors()
+        out[comm] = (losses, full_state_dict(model))
+        dist.barrier()
+    return out
+
+
+def test_peer_exchange_matches_collective_baseline():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = run_nccl(_peer_vs_nccl, 2)
+    for r in (0, 1):
+        lp, ln = res[r]["peer"][0], res[r]["nccl"][0]
+        assert lp == pytest.approx(ln, rel=2e-3, abs=2e-3)
+    sd_p, sd_n = res[0]["peer"][1], res[0]["nccl"][1]
+    for k in sd_n:
+        torch.testing.assert_close(sd_p[k], sd_n[k], rtol=2e-3, atol=2e-4, msg=lambda m: f"{k}: {m}")
+
+
+def _barrier_timeout(rank, world):
+    """A barrier whose peer never arrives returns an error status (no hang)."""
+    from primus_dlrm_b200.ops import _ext
+    from primus_dlrm_b200.parallel.sharded_embedding import SymmetricBuffer
+    dev = torch.device("cuda", rank)
+    pads = SymmetricBuffer(64 * 8, dev, rank, world)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ptrs = torch.tensor(pads.ptrs, dtype=torch.int64)
+    if rank == 0:  # only rank 0 enters: its wait for rank 1 must time out
+        _ext.core().signal_barrier(ptrs, rank, 5, int(0.5e9), err)
+    torch.cuda.synchronize()
+    import torch.distributed as dist
+    dist.barrier()
+    return int(err.item())
+
+
+def test_barrier_wait_is_bounded():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = run_nccl(_barrier_timeout, 2)
+    assert res[0] == 2 and res[1] == 0
