@@ -363,6 +363,7 @@ class PeerExecutor:
         cur = self.recv.get(dim)
         if cur is None or cur[1] < cap_rows:
             cap = max(int(cap_rows * 1.25), 1024)
+            cap = (cap + 63) // 64 * 64  # keeps the fp32 row block 16-byte aligned after the int64 keys
             nbytes = cap * 8 + cap * dim * 4
             if cur is None:
                 buf = SymmetricBuffer(nbytes, self.device, self.rank, self.world, self.group)
