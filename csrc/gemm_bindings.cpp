@@ -1,0 +1,17 @@
+// Python bindings of the primus_dlrm_b200 tensor-core kernels (module `_gemm`):
+// pyramid attention (attn_fmha.cu) and the tcgen05 GEMMs (gemm_*.cu).
+#include <torch/extension.h>
+
+namespace pd {
+std::vector<at::Tensor> fmha_fwd(at::Tensor, at::Tensor, at::Tensor, double);
+void fmha_bwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor,
+              at::Tensor, double);
+long long launches();
+}  // namespace pd
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "primus_dlrm_b200 sm_100a tensor-core kernels";
+  m.def("fmha_fwd", &pd::fmha_fwd, "pyramid causal attention forward -> (o, lse)");
+  m.def("fmha_bwd", &pd::fmha_bwd, "pyramid causal attention backward into dq/dk/dv views");
+  m.def("launch_count", &pd::launches);
+}

@@ -32,7 +32,9 @@ from primus_dlrm_b200.models.base import BaseModel
 from primus_dlrm_b200.models.embedding import Embeddings
 from primus_dlrm_b200.models.heads import fused_heads_loss
 from primus_dlrm_b200.ops import dense
-from primus_dlrm_b200.ops.attention import causal_attention_all_rows, pyramid_attention
+from primus_dlrm_b200.ops.attention import (
+    _native_ok as _fmha_native_ok, causal_attention_all_rows, pyramid_attention, pyramid_attention_qkv,
+)
 from primus_dlrm_b200.ops.embedding import SparseOptimizer
 from primus_dlrm_b200.ops.norm import add_norm, make_norm
 
@@ -80,6 +82,11 @@ class MixedAttention(nn.Module):
         B, T, D = x.shape
         qkv = dense.mixed_linear(x, n_s, self.s_qkv.weight, self.ns_qkv_weight)  # [B, T, 3D]
         qkv = qkv.view(B, T, 3, self.n_heads, self.d_head)
+        no_drop = not (self.training and self.attn_drop > 0 and self.attention_impl != "fav4")
+        if x.is_cuda and self.attention_impl in ("fav4", "fav2", "turbo", "native") and no_drop \
+                and _fmha_native_ok(qkv):
+            o = pyramid_attention_qkv(qkv, q_len)
+            return self.out_proj(o.reshape(B, q_len, D))
         if x.is_cuda and self.attention_impl in ("fav4", "fav2", "turbo", "native") and \
                 not (self.training and self.attn_drop > 0 and self.attention_impl != "fav4"):
             o = causal_attention_all_rows(qkv, self.n_heads).reshape(B, T, D)

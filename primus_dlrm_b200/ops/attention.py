@@ -36,6 +36,8 @@ def _native_ok(q: torch.Tensor) -> bool:
 
 
 class _NativeFMHA(torch.autograd.Function):
+    """q, k, v as separate [B, L, H, d] views (gradients returned separately)."""
+
     @staticmethod
     def forward(ctx, q, k, v, scale):
         G = _ext.gemm()
@@ -48,8 +50,46 @@ class _NativeFMHA(torch.autograd.Function):
     def backward(ctx, do):
         G = _ext.gemm()
         q, k, v, o, lse = ctx.saved_tensors
-        dq, dk, dv = G.fmha_bwd(q, k, v, o, lse, do.contiguous(), ctx.scale)
-        return dq, dk, dv, None
+        B, ql, H, d = q.shape
+        kl = k.shape[1]
+        buf = torch.empty(B, kl, 3, H, d, dtype=q.dtype, device=q.device)
+        G.fmha_bwd(q, k, v, o, lse, do.contiguous(), buf[:, :, 0], buf[:, :, 1], buf[:, :, 2], ctx.scale)
+        return buf[:, kl - ql:, 0], buf[:, :, 1], buf[:, :, 2], None
+
+
+class _NativeFMHAFused(torch.autograd.Function):
+    """Attention straight from the fused projection output qkv [B, T, 3, H, d]:
+    queries are the last q_len rows; the gradient is one [B, T, 3, H, d]
+    buffer written entirely by the backward kernels (no concatenation)."""
+
+    @staticmethod
+    def forward(ctx, qkv, q_len: int, scale: float):
+        G = _ext.gemm()
+        T = qkv.shape[1]
+        q, k, v = qkv[:, T - q_len:, 0], qkv[:, :, 1], qkv[:, :, 2]
+        o, lse = G.fmha_fwd(q, k, v, scale)
+        ctx.scale, ctx.q_len = scale, q_len
+        ctx.save_for_backward(qkv, o, lse)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        G = _ext.gemm()
+        qkv, o, lse = ctx.saved_tensors
+        T, ql = qkv.shape[1], ctx.q_len
+        dqkv = torch.empty_like(qkv)
+        G.fmha_bwd(qkv[:, T - ql:, 0], qkv[:, :, 1], qkv[:, :, 2], o, lse, do.contiguous(),
+                   dqkv[:, :, 0], dqkv[:, :, 1], dqkv[:, :, 2], ctx.scale)
+        return dqkv, None, None
+
+
+def pyramid_attention_qkv(qkv: torch.Tensor, q_len: int) -> torch.Tensor:
+    """qkv [B, T, 3, H, d] -> attention of the last q_len queries, [B, q_len, H, d]."""
+    d = qkv.shape[-1]
+    if _native_ok(qkv):
+        return _NativeFMHAFused.apply(qkv, q_len, d ** -0.5)
+    T = qkv.shape[1]
+    return pyramid_attention(qkv[:, T - q_len:, 0], qkv[:, :, 1], qkv[:, :, 2], impl="mask")
 
 
 def causal_attention_all_rows(qkv: torch.Tensor, n_heads: int) -> torch.Tensor:
