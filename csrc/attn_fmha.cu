@@ -108,7 +108,7 @@ constexpr int kFwdM = 128;  // queries per CTA (8 warps x 16)
 constexpr int kFwdN = 64;   // keys per tile
 
 template <int D>
-__global__ void __launch_bounds__(256) fmha_fwd_kernel(const FwdArgs A) {
+__global__ void __launch_bounds__(256, D == 32 ? 3 : 1) fmha_fwd_kernel(const FwdArgs A) {
   constexpr int NKS = D / 16;   // k-steps over d for QK^T
   constexpr int NDT = D / 8;    // n-tiles over d for PV
   __shared__ alignas(128) __nv_bfloat16 sQ[kFwdM * D];
@@ -283,7 +283,7 @@ struct BwdArgs {
   float scale_log2, scale;
 };
 
-// delta[b, h, i] = sum_d dO * O ; also zero the fp32 dQ accumulator
+// delta[b, h, i] = sum_d dO * O
 template <int D>
 __global__ void fmha_bwd_pre_kernel(const BwdArgs A) {
   const int bh = blockIdx.y, b = bh / A.H, h = bh % A.H;
@@ -298,9 +298,6 @@ __global__ void fmha_bwd_pre_kernel(const BwdArgs A) {
       s += a.x * d.x + a.y * d.y + a.z * d.z + a.w * d.w + a2.x * d2.x + a2.y * d2.y + a2.z * d2.z + a2.w * d2.w;
     }
     A.delta[(int64_t(b) * A.H + h) * A.q_len + i] = s;
-    float* dq = A.dq_acc + ((int64_t(b) * A.q_len + i) * A.H + h) * D;
-#pragma unroll
-    for (int c = 0; c < D; c += 4) *reinterpret_cast<float4*>(dq + c) = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
@@ -575,6 +572,7 @@ void fmha_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor
   if (B == 0) return;
   auto delta = at::empty({B, H, ql}, lse.options());
   auto dq_acc = at::empty({B, ql, H, D}, lse.options());
+  PD_CHECK_CUDA(cudaMemsetAsync(dq_acc.data_ptr(), 0, dq_acc.numel() * sizeof(float), stream()));
   attn::BwdArgs A{reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k.data_ptr()),
                   reinterpret_cast<const __nv_bfloat16*>(v.data_ptr()), q.stride(0), q.stride(1), k.stride(0), k.stride(1),
                   reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),

@@ -7,11 +7,16 @@ std::vector<at::Tensor> fmha_fwd(at::Tensor, at::Tensor, at::Tensor, double);
 void fmha_bwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor,
               at::Tensor, double);
 long long launches();
+void tc_gemm(at::Tensor, at::Tensor, at::Tensor, int64_t, c10::optional<at::Tensor>, c10::optional<at::Tensor>,
+             at::Tensor);
 }  // namespace pd
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "primus_dlrm_b200 sm_100a tensor-core kernels";
   m.def("fmha_fwd", &pd::fmha_fwd, "pyramid causal attention forward -> (o, lse)");
   m.def("fmha_bwd", &pd::fmha_bwd, "pyramid causal attention backward into dq/dk/dv views");
+  m.def("tc_gemm", &pd::tc_gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("epi") = 0,
+        py::arg("R") = py::none(), py::arg("AUX") = py::none(), py::arg("err"),
+        "C[l] = epi(A[l] @ B[l]^T) on tcgen05 (A [L,M,K], B [L|1,N,K], C [L,M,N] bf16 views)");
   m.def("launch_count", &pd::launches);
 }

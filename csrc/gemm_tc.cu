@@ -1,0 +1,437 @@
+// Persistent tcgen05 GEMM for sm_100a with fused epilogues.
+//
+//   C[l, m, n] = epi( sum_k A[l, m, k] * B[l, n, k] )        (A, B K-major, bf16)
+//
+// Structure (one CTA per SM, 6 warps):
+//   warp 0      TMA producer: A/B tiles (128 x 64 and BN x 64, 128-byte
+//               swizzle) into a STAGES-deep shared-memory ring, one mbarrier
+//               per stage with expected-transaction bytes.  No multicast.
+//   warp 1      allocates TMEM (2 x BN fp32 columns: a double-buffered
+//               accumulator) and one elected lane issues tcgen05.mma
+//               (M=128, N=BN, K=16 per instruction) for every k-step,
+//               releasing each smem stage with tcgen05.commit.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (each thread owns
+//               one accumulator row = one TMEM lane), apply the fused op,
+//               convert to bf16 and store; then hand the accumulator buffer
+//               back to the MMA warp.  The MMA of tile i+1 overlaps the
+//               epilogue of tile i.
+// Fused epilogues: none | GELU (optionally also storing the pre-activation) |
+// residual add | GELU backward (acc * gelu'(pre)).
+//
+// A and B are described by 3-D TMA maps {K, rows, L} with arbitrary row and
+// batch strides, so strided views (e.g. the NS rows of every sample, one
+// batch per NS token) are consumed in place; C / R / AUX take element strides.
+//
+// Every mbarrier wait is bounded (2 s on %globaltimer); on timeout the warp
+// records kWaitTimeout in the error word, stops issuing work, drains its own
+// in-flight operations (bounded) and the CTA frees its TMEM and exits.
+#include "common.cuh"
+
+#include <cuda.h>
+
+namespace pd {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+enum Epi : int { kNone = 0, kGelu = 1, kResidual = 2, kDGelu = 3 };
+
+struct Params {
+  int M, N, K, L;
+  int m_blocks, n_blocks, k_blocks, tiles;
+  __nv_bfloat16* C; int64_t c_ls, c_ms;
+  const __nv_bfloat16* R; int64_t r_ls, r_ms;      // residual (kResidual) or pre-activation (kDGelu)
+  __nv_bfloat16* AUX; int64_t aux_ls, aux_ms;       // pre-activation output (kGelu), optional
+  int epi;
+  int a_mode, b_mode;   // TMA map dim order: 0 = {K, rows, L}, 1 = {K, L, rows}
+  int b_shared;         // B has one batch shared by every l
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier --------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait: false (and the error word set) after kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err) {
+  if (mbar_try(b, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try(b, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_error(err, kWaitTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+// ---- TMA -------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2);
+// Load rows [row, row + box) of batch l; mode 1 maps have dims {K, L, rows}.
+__device__ __forceinline__ void tma_load_rows(void* dst, const CUtensorMap* map, uint64_t* bar, int mode, int k, int row,
+                                              int l) {
+  if (mode == 0) tma_load_3d(dst, map, bar, k, row, l);
+  else tma_load_3d(dst, map, bar, k, l, row);
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2) : "memory");
+}
+
+// ---- tcgen05 ---------------------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major, 128-byte-swizzled operand tile: rows of 64 bf16 (128 B), 8-row
+// atoms of 1024 B.  start advances by 32 B per 16-element k-step.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= uint64_t((addr >> 4) & 0x3FFF);        // start address
+  d |= uint64_t(1) << 16;                       // leading byte offset (unused for swizzled K-major)
+  d |= uint64_t(1024 >> 4) << 32;               // stride byte offset: 8 rows x 128 B
+  d |= uint64_t(1) << 46;                       // descriptor version (sm_100)
+  d |= uint64_t(2) << 61;                       // SWIZZLE_128B
+  return d;
+}
+// kind::f16 instruction descriptor: f32 accumulate, bf16 A/B, both K-major.
+__host__ __device__ constexpr uint32_t instr_desc(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc) : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tile_coords(const Params& p, int t, int& l, int& mb, int& nb) {
+  nb = t % p.n_blocks;
+  const int r = t / p.n_blocks;
+  mb = r % p.m_blocks;
+  l = r / p.m_blocks;
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                           const __grid_constant__ CUtensorMap tmB,
+                                                           const Params p) {
+  constexpr uint32_t kABytes = BM * BK * 2;
+  constexpr uint32_t kBBytes = BN * BK * 2;
+  constexpr uint32_t kTmemCols = 2 * BN;  // power of two for BN in {64, 128, 256}
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * kBBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;     // [2]
+  uint64_t* tempty = tfull + 2;         // [2]
+  uint64_t* mma_done = tempty + 2;      // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], kEpiWarps * 32); }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(tmem_slot)), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 1;
+      int issued = 0;
+      int issued_on[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) issued_on[s] = 0;
+      for (int t = blockIdx.x; t < p.tiles && !*abort_flag; t += gridDim.x) {
+        int l, mb, nb;
+        tile_coords(p, t, l, mb, nb);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase, p.err)) { *abort_flag = 1; break; }
+          mbar_expect_tx(&full[stage], kABytes + kBBytes);
+          tma_load_rows(sA + stage * kABytes, &tmA, &full[stage], p.a_mode, kb * BK, mb * BM, l);
+          tma_load_rows(sB + stage * kBBytes, &tmB, &full[stage], p.b_mode, kb * BK, nb * BN, p.b_shared ? 0 : l);
+          ++issued_on[stage];
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // drain: every issued load must have landed before the CTA can exit
+      if (*abort_flag) {
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s)
+          if (issued_on[s] > 0) (void)mbar_wait(&full[s], uint32_t(issued_on[s] - 1) & 1u, p.err);
+      }
+      (void)issued;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int t = blockIdx.x; t < p.tiles && !*abort_flag; t += gridDim.x, ++local) {
+        const int a = local & 1;
+        const uint32_t ephase = ((local >> 1) & 1) ^ 1;
+        if (!mbar_wait(&tempty[a], ephase, p.err)) { *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t d = tmem + uint32_t(a * BN);
+        bool ok = true;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) { *abort_flag = 1; ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * kBBytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            tc_mma(d, smem_desc(a_addr + k * 32), smem_desc(b_addr + k * 32), idesc, (kb | k) ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[a]);
+      }
+      // all MMAs issued by this thread have finished before TMEM is freed
+      tc_commit(mma_done);
+      (void)mbar_wait(mma_done, 0, p.err);
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;                     // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++local) {
+      const int a = local & 1;
+      if (!mbar_wait(&tfull[a], (local >> 1) & 1, p.err)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      int l, mb, nb;
+      tile_coords(p, t, l, mb, nb);
+      const int m = mb * BM + row_in_tile;
+      const bool row_ok = m < p.M;
+      const int n0 = nb * BN;
+      __nv_bfloat16* crow = p.C + l * p.c_ls + int64_t(m) * p.c_ms + n0;
+      const __nv_bfloat16* rrow = p.R ? p.R + l * p.r_ls + int64_t(m) * p.r_ms + n0 : nullptr;
+      __nv_bfloat16* arow = p.AUX ? p.AUX + l * p.aux_ls + int64_t(m) * p.aux_ms + n0 : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tc_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(a * BN + c), v);
+        if (!row_ok || n0 + c >= p.N) continue;
+        if (p.epi == kGelu && arow) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
+            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
+            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+            uint4 pk;
+            pk.x = *reinterpret_cast<uint32_t*>(&h0); pk.y = *reinterpret_cast<uint32_t*>(&h1);
+            pk.z = *reinterpret_cast<uint32_t*>(&h2); pk.w = *reinterpret_cast<uint32_t*>(&h3);
+            *reinterpret_cast<uint4*>(arow + c + j) = pk;
+          }
+        }
+        if (p.epi == kGelu) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_f(__bfloat162float(__float2bfloat16_rn(v[j])));
+        } else if (p.epi == kResidual) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 r = load4_bf16(rrow + c + j);
+            v[j] += r.x; v[j + 1] += r.y; v[j + 2] += r.z; v[j + 3] += r.w;
+          }
+        } else if (p.epi == kDGelu) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 r = load4_bf16(rrow + c + j);
+            v[j] *= gelu_grad_f(r.x); v[j + 1] *= gelu_grad_f(r.y);
+            v[j + 2] *= gelu_grad_f(r.z); v[j + 3] *= gelu_grad_f(r.w);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
+          __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
+          __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+          uint4 pk;
+          pk.x = *reinterpret_cast<uint32_t*>(&h0); pk.y = *reinterpret_cast<uint32_t*>(&h1);
+          pk.z = *reinterpret_cast<uint32_t*>(&h2); pk.w = *reinterpret_cast<uint32_t*>(&h3);
+          *reinterpret_cast<uint4*>(crow + c + j) = pk;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[a]);
+    }
+  }
+  // teardown: all roles are out of their loops (every wait above is bounded)
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+}  // namespace tc
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+
+// 3-D tensor map over bf16 rows of length K (strides in elements).  mode 0:
+// dims {K, rows, L}; mode 1 (batch stride smaller than the row stride, e.g.
+// one batch per NS token): dims {K, L, rows} so the strides stay ascending.
+CUtensorMap make_map(const void* base, int64_t K, int64_t rows, int64_t L, int64_t row_stride, int64_t l_stride,
+                     int box_rows, int& mode) {
+  CUtensorMap m;
+  if (L <= 1) l_stride = row_stride * rows;
+  mode = (L > 1 && l_stride < row_stride) ? 1 : 0;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3];
+  if (mode == 0) {
+    dims[0] = K; dims[1] = rows; dims[2] = L;
+    strides[0] = row_stride * 2; strides[1] = l_stride * 2;
+    box[0] = tc::BK; box[1] = box_rows; box[2] = 1;
+  } else {
+    dims[0] = K; dims[1] = L; dims[2] = rows;
+    strides[0] = l_stride * 2; strides[1] = row_stride * 2;
+    box[0] = tc::BK; box[1] = 1; box[2] = box_rows;
+  }
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = cuTensorMapEncodeTiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", int(r), "): K=", K, " rows=", rows, " L=", L,
+              " row_stride=", row_stride, " l_stride=", l_stride);
+  return m;
+}
+
+// [L, rows, K] view (L may be 1): unit stride on K, 16-byte aligned rows.
+void check_operand(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, ": bf16 CUDA tensor required");
+  TORCH_CHECK(t.dim() == 3 && t.stride(2) == 1, name, ": [L, rows, K] with unit stride on K required");
+  TORCH_CHECK(t.stride(1) % 8 == 0 && (t.size(0) == 1 || t.stride(0) % 8 == 0) &&
+              reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, ": rows must be 16-byte aligned");
+  TORCH_CHECK(t.size(2) % 8 == 0, name, ": K must be a multiple of 8");
+}
+
+template <int BN, int STAGES>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const tc::Params& p) {
+  constexpr size_t smem = STAGES * (tc::BM * tc::BK * 2 + BN * tc::BK * 2) + 1024 + 512;
+  static bool attr = false;
+  if (!attr) {
+    PD_CHECK_CUDA(cudaFuncSetAttribute(tc::gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(smem)));
+    attr = true;
+  }
+  int grid = p.tiles < num_sms() ? p.tiles : num_sms();
+  tc::gemm_kernel<BN, STAGES><<<grid, tc::kThreads, smem, stream()>>>(ta, tb, p);
+  PD_CHECK_LAUNCH();
+}
+
+}  // namespace
+
+// C[l, m, :N] = epi(A[l] @ B[l]^T).  A: [L, M, K], B: [L or 1, N, K], C/R/AUX: [L, M, N] views
+// (unit column stride).  epi: 0 none, 1 gelu (aux = pre-activation, optional), 2 residual (R),
+// 3 dgelu (R = pre-activation).
+void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optional<at::Tensor> R,
+             c10::optional<at::Tensor> AUX, at::Tensor err) {
+  check_operand(A, "A");
+  check_operand(B, "B");
+  const int64_t L = A.size(0), M = A.size(1), K = A.size(2), N = B.size(1);
+  TORCH_CHECK(B.size(2) == K && (B.size(0) == L || B.size(0) == 1), "B must be [L or 1, N, K]");
+  TORCH_CHECK(N % 64 == 0, "N must be a multiple of 64");
+  TORCH_CHECK(C.dim() == 3 && C.size(0) == L && C.size(1) == M && C.size(2) == N && C.stride(2) == 1 &&
+              C.scalar_type() == at::kBFloat16 && C.stride(1) % 8 == 0 &&
+              reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0, "C must be a [L, M, N] bf16 view with aligned rows");
+  tc::Params p{};
+  p.M = int(M); p.N = int(N); p.K = int(K); p.L = int(L);
+  p.m_blocks = int((M + tc::BM - 1) / tc::BM);
+  p.k_blocks = int((K + tc::BK - 1) / tc::BK);
+  p.C = reinterpret_cast<__nv_bfloat16*>(C.data_ptr()); p.c_ls = C.stride(0); p.c_ms = C.stride(1);
+  p.epi = int(epi);
+  p.err = err.data_ptr<int>();
+  if (epi == tc::kResidual || epi == tc::kDGelu) {
+    TORCH_CHECK(R && R->dim() == 3 && R->sizes() == C.sizes() && R->stride(2) == 1 && R->stride(1) % 8 == 0 &&
+                R->scalar_type() == at::kBFloat16, "R must match C");
+    p.R = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr()); p.r_ls = R->stride(0); p.r_ms = R->stride(1);
+  }
+  if (AUX && AUX->defined()) {
+    TORCH_CHECK(AUX->dim() == 3 && AUX->sizes() == C.sizes() && AUX->stride(2) == 1 && AUX->stride(1) % 8 == 0);
+    p.AUX = reinterpret_cast<__nv_bfloat16*>(AUX->data_ptr()); p.aux_ls = AUX->stride(0); p.aux_ms = AUX->stride(1);
+  }
+  if (M == 0 || L == 0) return;
+  const int BN = (N % 256 == 0) ? 256 : (N % 128 == 0 ? 128 : 64);
+  p.n_blocks = int(N / BN);
+  p.tiles = int(L) * p.m_blocks * p.n_blocks;
+  const CUtensorMap ta = make_map(A.data_ptr(), K, M, L, A.stride(1), A.stride(0), tc::BM, p.a_mode);
+  const CUtensorMap tb = make_map(B.data_ptr(), K, N, B.size(0), B.stride(1), B.stride(0), BN, p.b_mode);
+  p.b_shared = (B.size(0) == 1) ? 1 : 0;
+  if (BN == 256) launch<256, 4>(ta, tb, p);
+  else if (BN == 128) launch<128, 6>(ta, tb, p);
+  else launch<64, 8>(ta, tb, p);
+}
+
+}  // namespace pd

@@ -141,6 +141,10 @@ class OneTransBlock(nn.Module):
         x_tail = x[:, kv_len - q_len:]
         y, z = add_norm(a, x_tail, self.norm2.weight,
                         getattr(self.norm2, "bias", None), self.norm2.eps, self.norm2.kind)
+        fused = dense.mixed_ffn(y, z, q_len - n_ns, self.ffn.s_w1.weight, self.ffn.s_w2.weight,
+                                self.ffn.ns_w1, self.ffn.ns_w2) if (self.ffn.dropout.p == 0 or not self.training) else None
+        if fused is not None:
+            return fused
         f = self.ffn(y, n_s=q_len - n_ns)
         return z + f
 

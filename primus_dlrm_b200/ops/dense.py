@@ -26,35 +26,145 @@ def _gemm_ok(x: torch.Tensor) -> bool:
     if not (x.is_cuda and _ext.native_enabled(x.device)):
         return False
     g = _ext.gemm()
-    return g is not None and hasattr(g, "mixed_linear_fwd")
+    return g is not None and hasattr(g, "tc_gemm")
 
 
 def _cast_w(w: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
     return w.to(like.dtype) if w.dtype != like.dtype else w
 
 
+_EPI = {"": 0, None: 0, "gelu": 1, "residual": 2, "dgelu": 3}
+_err_words: dict = {}
+
+
+def _err(device) -> torch.Tensor:
+    e = _err_words.get(device)
+    if e is None:
+        e = torch.zeros(1, dtype=torch.int32, device=device)
+        _err_words[device] = e
+    return e
+
+
+def gemm_error_code(device) -> int:
+    """Error word of the tcgen05 GEMMs on ``device`` (2 = a pipeline wait timed out)."""
+    e = _err_words.get(torch.device(device))
+    return int(e.item()) if e is not None else 0
+
+
+def tc_gemm(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, epi: str | None = None,
+            R: torch.Tensor | None = None, AUX: torch.Tensor | None = None) -> torch.Tensor:
+    """C[l] = epi(A[l] @ B[l]^T) on the sm_100a tcgen05 kernel; A [L, M, K],
+    B [L or 1, N, K], C/R/AUX [L, M, N] (bf16 views, unit stride on the last dim)."""
+    _ext.gemm().tc_gemm(A, B, C, _EPI[epi], R, AUX, _err(A.device))
+    return C
+
+
+def _tc_ok(x: torch.Tensor, K: int, N: int) -> bool:
+    return x.dtype == torch.bfloat16 and K % 8 == 0 and N % 64 == 0 and x.data_ptr() % 16 == 0
+
+
+def _mixed_tc(x, n_s, ws, wn, out, epi=None, R=None, AUX=None):
+    """out = epi(mixed(x)) with the tcgen05 GEMM: all T rows with ws, then the
+    NS rows (one batch per token) with wn.  x [B, T, K]; ws [N, K]; wn [NS, N, K]."""
+    Bsz, T, K = x.shape
+    N = ws.shape[0]
+    v = lambda t: t.reshape(1, Bsz * T, t.shape[-1]) if t is not None else None
+    tc_gemm(v(x), ws.reshape(1, N, K), v(out), epi, v(R), v(AUX))
+    if T > n_s:
+        tr = lambda t: t[:, n_s:].transpose(0, 1) if t is not None else None
+        tc_gemm(tr(x), wn, tr(out), epi, tr(R), tr(AUX))
+    return out
+
+
+def _dw(dy, x, n_s, wdt):
+    """Weight gradients of a mixed projection (cuBLAS): shared S weight from
+    the first n_s rows of every sample, per-token NS weights."""
+    B, T, N = dy.shape
+    K = x.shape[-1]
+    dws = torch.matmul(dy.reshape(-1, N).t(), x.reshape(-1, K)).float()
+    if T > n_s:
+        dwn = torch.einsum("btm,btn->tmn", dy[:, n_s:], x[:, n_s:]).float()
+        dws -= dwn.sum(0)
+    else:
+        dwn = torch.zeros(0, N, K, device=dy.device)
+    return dws.to(wdt[0]), dwn.to(wdt[1])
+
+
 class _MixedLinearNative(torch.autograd.Function):
-    """tcgen05 grouped GEMM: one launch for the shared S rows + all NS tokens."""
+    """Mixed projection on the tcgen05 GEMM (GELU fused into the epilogue)."""
 
     @staticmethod
     def forward(ctx, x, w_s, w_ns, n_s: int, act: str):
-        G = _ext.gemm()
         xb = x.contiguous()
-        wsb = w_s.to(torch.bfloat16)
-        wnb = w_ns.to(torch.bfloat16)
-        y, pre = G.mixed_linear_fwd(xb, wsb, wnb, n_s, act == "gelu")
-        ctx.save_for_backward(xb, wsb, wnb, pre if act == "gelu" else y.new_empty(0))
-        ctx.n_s, ctx.act = n_s, act
-        ctx.w_dtypes = (w_s.dtype, w_ns.dtype)
+        ws, wn = w_s.to(torch.bfloat16), w_ns.to(torch.bfloat16)
+        B, T, _ = xb.shape
+        N = ws.shape[0]
+        y = torch.empty(B, T, N, dtype=torch.bfloat16, device=x.device)
+        pre = torch.empty_like(y) if act == "gelu" else None
+        _mixed_tc(xb, n_s, ws, wn, y, "gelu" if act == "gelu" else None, AUX=pre)
+        ctx.save_for_backward(xb, ws, wn, pre if pre is not None else y.new_empty(0))
+        ctx.n_s, ctx.act, ctx.wdt = n_s, act, (w_s.dtype, w_ns.dtype)
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        G = _ext.gemm()
-        xb, wsb, wnb, pre = ctx.saved_tensors
-        dx, dws, dwn = G.mixed_linear_bwd(dy.contiguous().to(torch.bfloat16), xb, wsb, wnb,
-                                          pre if ctx.act == "gelu" else None, ctx.n_s)
-        return dx, dws.to(ctx.w_dtypes[0]), dwn.to(ctx.w_dtypes[1]), None, None
+        xb, ws, wn, pre = ctx.saved_tensors
+        dy = dy.contiguous().to(torch.bfloat16)
+        if ctx.act == "gelu":
+            dy = torch.ops.aten.gelu_backward(dy, pre)
+        B, T, K = xb.shape
+        dx = torch.empty(B, T, K, dtype=torch.bfloat16, device=xb.device)
+        _mixed_tc(dy, ctx.n_s, ws.t().contiguous(), wn.transpose(1, 2).contiguous(), dx)
+        dws, dwn = _dw(dy, xb, ctx.n_s, ctx.wdt)
+        return dx, dws, dwn, None, None
+
+
+class MixedFFNNative(torch.autograd.Function):
+    """out = z + W2(GELU(W1 x)) for the mixed S / NS parameterisation, on the
+    tcgen05 GEMM: GELU (+ pre-activation store) fused into the up projection,
+    the residual add into the down projection, and GELU's backward into the
+    down projection's data-gradient GEMM."""
+
+    @staticmethod
+    def forward(ctx, x, z, w1, w2, wn1, wn2, n_s: int):
+        xb = x.contiguous()
+        bw = [w.to(torch.bfloat16) for w in (w1, w2, wn1, wn2)]
+        B, T, D = xb.shape
+        F_ = bw[0].shape[0]
+        h = torch.empty(B, T, F_, dtype=torch.bfloat16, device=x.device)
+        pre = torch.empty_like(h)
+        _mixed_tc(xb, n_s, bw[0], bw[2], h, "gelu", AUX=pre)
+        out = torch.empty(B, T, D, dtype=torch.bfloat16, device=x.device)
+        _mixed_tc(h, n_s, bw[1], bw[3], out, "residual", R=z)
+        ctx.save_for_backward(xb, h, pre, *bw)
+        ctx.n_s = n_s
+        ctx.wdt = [w.dtype for w in (w1, w2, wn1, wn2)]
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        xb, h, pre, w1, w2, wn1, wn2 = ctx.saved_tensors
+        n_s = ctx.n_s
+        dout = dout.contiguous().to(torch.bfloat16)
+        B, T, D = xb.shape
+        F_ = w1.shape[0]
+        dpre = torch.empty(B, T, F_, dtype=torch.bfloat16, device=xb.device)
+        _mixed_tc(dout, n_s, w2.t().contiguous(), wn2.transpose(1, 2).contiguous(), dpre, "dgelu", R=pre)
+        dw2, dwn2 = _dw(dout, h, n_s, (ctx.wdt[1], ctx.wdt[3]))
+        dx = torch.empty(B, T, D, dtype=torch.bfloat16, device=xb.device)
+        _mixed_tc(dpre, n_s, w1.t().contiguous(), wn1.transpose(1, 2).contiguous(), dx)
+        dw1, dwn1 = _dw(dpre, xb, n_s, (ctx.wdt[0], ctx.wdt[2]))
+        return dx, dout, dw1, dw2, dwn1, dwn2, None
+
+
+def mixed_ffn(x: torch.Tensor, z: torch.Tensor, n_s: int, w1, w2, wn1, wn2) -> torch.Tensor | None:
+    """Fused native FFN + residual, or None when the native GEMM cannot run it."""
+    if not (_gemm_ok(x) and x.dtype == torch.bfloat16 and z.dtype == torch.bfloat16):
+        return None
+    D, F_ = w2.shape[0], w1.shape[0]
+    if not (_tc_ok(x, D, F_) and F_ % 64 == 0 and D % 64 == 0 and z.stride(-1) == 1 and z.stride(-2) % 8 == 0):
+        return None
+    return MixedFFNNative.apply(x, z, w1, w2, wn1, wn2, n_s)
 
 
 class _MixedLinearTorch(torch.autograd.Function):
@@ -92,7 +202,7 @@ class _MixedLinearTorch(torch.autograd.Function):
         if T > n_s:
             dy_ns, x_ns = dy[:, n_s:], x[:, n_s:]
             dx[:, n_s:] = torch.einsum("btm,tmn->btn", dy_ns, wn)
-            dwn = torch.einsum("btm,btn->tmn", dy_ns.float(), x_ns.float())
+            dwn = torch.einsum("btm,btn->tmn", dy_ns, x_ns).float()
             dws -= dwn.sum(0)
         else:
             dwn = torch.zeros(wn.shape, dtype=torch.float32, device=x.device)
@@ -102,7 +212,7 @@ class _MixedLinearTorch(torch.autograd.Function):
 def mixed_linear(x: torch.Tensor, n_s: int, w_s: torch.Tensor, w_ns: torch.Tensor,
                  act: str | None = None) -> torch.Tensor:
     """x [B, T, Din] -> [B, T, Dout]; rows < n_s use w_s [Dout, Din], row n_s+t uses w_ns[t]."""
-    if _gemm_ok(x) and x.dtype == torch.bfloat16:
+    if _gemm_ok(x) and _tc_ok(x, x.shape[-1], w_s.shape[0]):
         return _MixedLinearNative.apply(x, w_s, w_ns, n_s, act or "")
     if x.is_cuda and x.dtype == torch.bfloat16:
         return _MixedLinearTorch.apply(x, w_s, w_ns, n_s, act or "")

@@ -1,0 +1,83 @@
+"""tcgen05 GEMM (sm_100a) vs fp32 PyTorch matmul, incl. strided batched views
+and the fused epilogues."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf(*s):
+    return torch.randn(*s, device="cuda").to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K", [(1000, 768, 256), (128, 256, 1024), (129, 128, 64), (4099, 1024, 256),
+                                   (77, 64, 192), (2048, 256, 512)])
+def test_plain(M, N, K):
+    from primus_dlrm_b200.ops.dense import tc_gemm, gemm_error_code
+    a, b = _bf(1, M, K), _bf(1, N, K)
+    c = torch.empty(1, M, N, device="cuda", dtype=torch.bfloat16)
+    tc_gemm(a, b, c)
+    ref = a.float() @ b.float().transpose(1, 2)
+    torch.testing.assert_close(c.float(), ref, rtol=2e-2, atol=2e-2 * K ** 0.5)
+    assert gemm_error_code("cuda") == 0
+
+
+def test_batched_strided_ns_layout():
+    """NS rows of every sample as one batch per token (row stride T*K, batch stride K)."""
+    from primus_dlrm_b200.ops.dense import tc_gemm
+    Bsz, T, n_s, K, N = 300, 40, 24, 256, 768
+    x = _bf(Bsz, T, K)
+    w = _bf(T - n_s, N, K)
+    y = torch.zeros(Bsz, T, N, device="cuda", dtype=torch.bfloat16)
+    tc_gemm(x[:, n_s:].transpose(0, 1), w, y[:, n_s:].transpose(0, 1))
+    ref = torch.einsum("btk,tnk->btn", x[:, n_s:].float(), w.float())
+    torch.testing.assert_close(y[:, n_s:].float(), ref, rtol=2e-2, atol=0.35)
+    assert torch.all(y[:, :n_s] == 0)
+
+
+def test_epilogues():
+    from primus_dlrm_b200.ops.dense import tc_gemm
+    M, N, K = 700, 256, 256
+    a, b = _bf(1, M, K), _bf(1, N, K)
+    acc = a.float() @ b.float().transpose(1, 2)
+    pre_b = acc.to(torch.bfloat16)
+    c = torch.empty(1, M, N, device="cuda", dtype=torch.bfloat16)
+    aux = torch.empty_like(c)
+    tc_gemm(a, b, c, "gelu", AUX=aux)
+    torch.testing.assert_close(aux.float(), pre_b.float(), rtol=2e-2, atol=0.3)
+    torch.testing.assert_close(c.float(), F.gelu(aux.float()), rtol=2e-2, atol=2e-2)
+    r = _bf(1, M, N)
+    tc_gemm(a, b, c, "residual", R=r)
+    torch.testing.assert_close(c.float(), acc + r.float(), rtol=2e-2, atol=0.35)
+    tc_gemm(a, b, c, "dgelu", R=r)
+    x = r.float().requires_grad_(True)
+    F.gelu(x).backward(torch.ones_like(x))
+    torch.testing.assert_close(c.float(), acc * x.grad, rtol=3e-2, atol=0.5)
+
+
+def test_mixed_linear_and_ffn_match_torch_path():
+    import os
+
+    from primus_dlrm_b200.ops import dense
+    torch.manual_seed(0)
+    Bsz, T, n_s, D, F_ = 64, 40, 24, 256, 1024
+    x = (_bf(Bsz, T, D) * 0.5).requires_grad_(True)
+    z = _bf(Bsz, T, D).requires_grad_(True)
+    w1 = (torch.randn(F_, D, device="cuda") * 0.05).requires_grad_(True)
+    w2 = (torch.randn(D, F_, device="cuda") * 0.05).requires_grad_(True)
+    wn1 = (torch.randn(T - n_s, F_, D, device="cuda") * 0.05).requires_grad_(True)
+    wn2 = (torch.randn(T - n_s, D, F_, device="cuda") * 0.05).requires_grad_(True)
+    out = dense.mixed_ffn(x, z, n_s, w1, w2, wn1, wn2)
+    assert out is not None
+    g = torch.randn_like(out)
+    out.backward(g)
+    got = [t.grad.clone() for t in (x, z, w1, w2, wn1, wn2)]
+    for t in (x, z, w1, w2, wn1, wn2):
+        t.grad = None
+    h = dense._MixedLinearTorch.apply(x, w1, wn1, n_s, "gelu")
+    ref = z + dense._MixedLinearTorch.apply(h, w2, wn2, n_s, "")
+    torch.testing.assert_close(out.float(), ref.float(), rtol=3e-2, atol=3e-2)
+    ref.backward(g)
+    for a, b in zip(got, (x.grad, z.grad, w1.grad, w2.grad, wn1.grad, wn2.grad)):
+        torch.testing.assert_close(a.float(), b.float(), rtol=5e-2, atol=5e-2 * (b.float().abs().max().item() + 1e-3))
