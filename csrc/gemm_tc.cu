@@ -34,7 +34,7 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;   // two warps per TMEM lane quarter, splitting the columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
@@ -171,6 +171,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   uint64_t* tempty = tfull + 2;         // [2]
   uint64_t* mma_done = tempty + 2;      // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  // per epilogue warp: 32 x 32 bf16 staging blocks for C and R / AUX (64-byte
+  // rows, 16-byte chunks XOR-swizzled by (row >> 1) & 3: conflict-free both
+  // when a thread writes its own row and when 4 lanes cover one row)
+  uint8_t* stage_base = reinterpret_cast<uint8_t*>(tmem_slot) + 64;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -258,8 +262,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
   } else {
     // ---------------- epilogue ----------------
+    const int ew = warp - 2;                    // epilogue warp 0..7
     const int q = warp & 3;                     // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;
+    const int half = ew >> 2;                   // which half of the columns
+    uint8_t* stC = stage_base + ew * 2 * 2048;
+    uint8_t* stR = stC + 2048;
+    uint8_t* stX = stR;   // GELU (AUX) and residual/dGELU (R) never occur together
+    // lane -> (row, 16-byte chunk) for the cooperative, coalesced row copies
+    const int cr = lane >> 2, cc = lane & 3;
+    auto sw = [](int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); };
     int local = 0;
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++local) {
       const int a = local & 1;
@@ -267,58 +278,78 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       tc_fence_after();
       int l, mb, nb;
       tile_coords(p, t, l, mb, nb);
-      const int m = mb * BM + row_in_tile;
-      const bool row_ok = m < p.M;
+      const int m0 = mb * BM + q * 32;          // first row of this warp's 32-row slab
       const int n0 = nb * BN;
-      __nv_bfloat16* crow = p.C + l * p.c_ls + int64_t(m) * p.c_ms + n0;
-      const __nv_bfloat16* rrow = p.R ? p.R + l * p.r_ls + int64_t(m) * p.r_ms + n0 : nullptr;
-      __nv_bfloat16* arow = p.AUX ? p.AUX + l * p.aux_ls + int64_t(m) * p.aux_ms + n0 : nullptr;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+        // residual / pre-activation block -> smem (coalesced 64-byte rows)
+        if (p.epi == kResidual || p.epi == kDGelu) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = cr + 8 * i;
+            uint4 val = make_uint4(0, 0, 0, 0);
+            if (m0 + r < p.M)
+              val = *reinterpret_cast<const uint4*>(p.R + l * p.r_ls + int64_t(m0 + r) * p.r_ms + n0 + c + cc * 8);
+            *reinterpret_cast<uint4*>(stR + sw(r, cc)) = val;
+          }
+          __syncwarp();
+        }
         float v[32];
         tc_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(a * BN + c), v);
-        if (!row_ok || n0 + c >= p.N) continue;
-        if (p.epi == kGelu && arow) {
+        if (p.epi == kGelu && p.AUX) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
-            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
-            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+          for (int j = 0; j < 4; ++j) {
             uint4 pk;
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[8 * j], v[8 * j + 1]);
+            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 * j + 2], v[8 * j + 3]);
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * j + 4], v[8 * j + 5]);
+            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[8 * j + 6], v[8 * j + 7]);
             pk.x = *reinterpret_cast<uint32_t*>(&h0); pk.y = *reinterpret_cast<uint32_t*>(&h1);
             pk.z = *reinterpret_cast<uint32_t*>(&h2); pk.w = *reinterpret_cast<uint32_t*>(&h3);
-            *reinterpret_cast<uint4*>(arow + c + j) = pk;
+            *reinterpret_cast<uint4*>(stX + sw(lane, j)) = pk;
           }
         }
         if (p.epi == kGelu) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu_f(__bfloat162float(__float2bfloat16_rn(v[j])));
-        } else if (p.epi == kResidual) {
+        } else if (p.epi == kResidual || p.epi == kDGelu) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 r = load4_bf16(rrow + c + j);
-            v[j] += r.x; v[j + 1] += r.y; v[j + 2] += r.z; v[j + 3] += r.w;
-          }
-        } else if (p.epi == kDGelu) {
+          for (int j = 0; j < 4; ++j) {
+            const uint4 pk = *reinterpret_cast<const uint4*>(stR + sw(lane, j));
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&pk);
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 r = load4_bf16(rrow + c + j);
-            v[j] *= gelu_grad_f(r.x); v[j + 1] *= gelu_grad_f(r.y);
-            v[j + 2] *= gelu_grad_f(r.z); v[j + 3] *= gelu_grad_f(r.w);
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __bfloat1622float2(h[e]);
+              if (p.epi == kResidual) { v[8 * j + 2 * e] += f.x; v[8 * j + 2 * e + 1] += f.y; }
+              else { v[8 * j + 2 * e] *= gelu_grad_f(f.x); v[8 * j + 2 * e + 1] *= gelu_grad_f(f.y); }
+            }
           }
         }
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
-          __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
-          __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+        for (int j = 0; j < 4; ++j) {
           uint4 pk;
+          __nv_bfloat162 h0 = __floats2bfloat162_rn(v[8 * j], v[8 * j + 1]);
+          __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 * j + 2], v[8 * j + 3]);
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * j + 4], v[8 * j + 5]);
+          __nv_bfloat162 h3 = __floats2bfloat162_rn(v[8 * j + 6], v[8 * j + 7]);
           pk.x = *reinterpret_cast<uint32_t*>(&h0); pk.y = *reinterpret_cast<uint32_t*>(&h1);
           pk.z = *reinterpret_cast<uint32_t*>(&h2); pk.w = *reinterpret_cast<uint32_t*>(&h3);
-          *reinterpret_cast<uint4*>(crow + c + j) = pk;
+          *reinterpret_cast<uint4*>(stC + sw(lane, j)) = pk;
         }
+        __syncwarp();
+        // coalesced stores: 4 lanes cover one 64-byte row segment, 8 rows per pass
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = cr + 8 * i;
+          if (m0 + r < p.M) {
+            *reinterpret_cast<uint4*>(p.C + l * p.c_ls + int64_t(m0 + r) * p.c_ms + n0 + c + cc * 8) =
+                *reinterpret_cast<const uint4*>(stC + sw(r, cc));
+            if (p.epi == kGelu && p.AUX)
+              *reinterpret_cast<uint4*>(p.AUX + l * p.aux_ls + int64_t(m0 + r) * p.aux_ms + n0 + c + cc * 8) =
+                  *reinterpret_cast<const uint4*>(stX + sw(r, cc));
+          }
+        }
+        __syncwarp();
       }
       tc_fence_before();
       mbar_arrive(&tempty[a]);
@@ -379,7 +410,7 @@ void check_operand(const at::Tensor& t, const char* name) {
 
 template <int BN, int STAGES>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const tc::Params& p) {
-  constexpr size_t smem = STAGES * (tc::BM * tc::BK * 2 + BN * tc::BK * 2) + 1024 + 512;
+  constexpr size_t smem = STAGES * (tc::BM * tc::BK * 2 + BN * tc::BK * 2) + 1024 + 512 + tc::kEpiWarps * 2 * 2048;
   static bool attr = false;
   if (!attr) {
     PD_CHECK_CUDA(cudaFuncSetAttribute(tc::gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
