@@ -174,7 +174,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   // per epilogue warp: 32 x 32 bf16 staging blocks for C and R / AUX (64-byte
   // rows, 16-byte chunks XOR-swizzled by (row >> 1) & 3: conflict-free both
   // when a thread writes its own row and when 4 lanes cover one row)
-  uint8_t* stage_base = reinterpret_cast<uint8_t*>(tmem_slot) + 64;
+  uint8_t* stage_base = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(tmem_slot) + 64 + 127) & ~uintptr_t(127));  // 16-byte vector accesses
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -435,7 +436,7 @@ void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optiona
   TORCH_CHECK(B.size(2) == K && (B.size(0) == L || B.size(0) == 1), "B must be [L or 1, N, K]");
   TORCH_CHECK(N % 64 == 0, "N must be a multiple of 64");
   TORCH_CHECK(C.dim() == 3 && C.size(0) == L && C.size(1) == M && C.size(2) == N && C.stride(2) == 1 &&
-              C.scalar_type() == at::kBFloat16 && C.stride(1) % 8 == 0 &&
+              C.scalar_type() == at::kBFloat16 && C.stride(1) % 8 == 0 && (C.size(0) == 1 || C.stride(0) % 8 == 0) &&
               reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0, "C must be a [L, M, N] bf16 view with aligned rows");
   tc::Params p{};
   p.M = int(M); p.N = int(N); p.K = int(K); p.L = int(L);
@@ -446,11 +447,14 @@ void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optiona
   p.err = err.data_ptr<int>();
   if (epi == tc::kResidual || epi == tc::kDGelu) {
     TORCH_CHECK(R && R->dim() == 3 && R->sizes() == C.sizes() && R->stride(2) == 1 && R->stride(1) % 8 == 0 &&
-                R->scalar_type() == at::kBFloat16, "R must match C");
+                (R->size(0) == 1 || R->stride(0) % 8 == 0) && reinterpret_cast<uintptr_t>(R->data_ptr()) % 16 == 0 &&
+                R->scalar_type() == at::kBFloat16, "R must match C (bf16, 16-byte aligned rows)");
     p.R = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr()); p.r_ls = R->stride(0); p.r_ms = R->stride(1);
   }
   if (AUX && AUX->defined()) {
-    TORCH_CHECK(AUX->dim() == 3 && AUX->sizes() == C.sizes() && AUX->stride(2) == 1 && AUX->stride(1) % 8 == 0);
+    TORCH_CHECK(AUX->dim() == 3 && AUX->sizes() == C.sizes() && AUX->stride(2) == 1 && AUX->stride(1) % 8 == 0 &&
+                (AUX->size(0) == 1 || AUX->stride(0) % 8 == 0) && reinterpret_cast<uintptr_t>(AUX->data_ptr()) % 16 == 0,
+                "AUX must match C (16-byte aligned rows)");
     p.AUX = reinterpret_cast<__nv_bfloat16*>(AUX->data_ptr()); p.aux_ls = AUX->stride(0); p.aux_ms = AUX->stride(1);
   }
   if (M == 0 || L == 0) return;
