@@ -101,14 +101,30 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// GELU (tanh-free exact form via erf), shared by epilogues and tokenizers.
-__device__ __forceinline__ float gelu_f(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+// GELU(x) = x * Phi(x) (the exact, erf-based form used by nn.GELU()).
+// erf is evaluated with Abramowitz & Stegun, Handbook of Mathematical
+// Functions (1964), formula 7.1.26: erf(x) = 1 - (a1 t + ... + a5 t^5) e^{-x^2},
+// t = 1 / (1 + p x), |error| <= 1.5e-7 -- far below bf16 resolution.  The same
+// exponential gives the Gaussian density for GELU's derivative, so one
+// reciprocal and one exponential cover both.
+struct GeluEval { float cdf, pdf; };
+__device__ __forceinline__ GeluEval gelu_eval(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;               // |x| / sqrt(2)
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+  float poly = fmaf(1.061405429f, t, -1.453152027f);
+  poly = fmaf(poly, t, 1.421413741f);
+  poly = fmaf(poly, t, -0.284496736f);
+  poly = fmaf(poly, t, 0.254829592f);
+  poly *= t;
+  const float e = __expf(-z * z);                                   // exp(-x^2 / 2)
+  const float erf_abs = 1.0f - poly * e;
+  const float erf_v = x < 0.f ? -erf_abs : erf_abs;
+  return GeluEval{0.5f * (1.0f + erf_v), 0.3989422804014327f * e};  // Phi(x), phi(x)
 }
+__device__ __forceinline__ float gelu_f(float x) { return x * gelu_eval(x).cdf; }
 __device__ __forceinline__ float gelu_grad_f(float x) {
-  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752f));
-  const float pdf = 0.3989422804014327f * __expf(-0.5f * x * x);
-  return cdf + x * pdf;
+  const GeluEval g = gelu_eval(x);
+  return g.cdf + x * g.pdf;
 }
 
 }  // namespace pd

@@ -81,3 +81,28 @@ def test_mixed_linear_and_ffn_match_torch_path():
     ref.backward(g)
     for a, b in zip(got, (x.grad, z.grad, w1.grad, w2.grad, wn1.grad, wn2.grad)):
         torch.testing.assert_close(a.float(), b.float(), rtol=5e-2, atol=5e-2 * (b.float().abs().max().item() + 1e-3))
+
+
+def test_gelu_epilogue_accuracy_vs_exact_erf():
+    """The GEMM's GELU / GELU' (Abramowitz-Stegun erf) against torch's exact erf GELU."""
+    from primus_dlrm_b200.ops.dense import tc_gemm
+    M, N, K = 256, 256, 64
+    # A = identity-like rows so the accumulator equals a chosen value per column
+    vals = torch.linspace(-8, 8, N, device="cuda")
+    a = torch.zeros(1, M, K, device="cuda")
+    a[0, :, 0] = 1.0
+    b = torch.zeros(1, N, K, device="cuda")
+    b[0, :, 0] = vals
+    a, b = a.to(torch.bfloat16), b.to(torch.bfloat16)
+    c = torch.empty(1, M, N, device="cuda", dtype=torch.bfloat16)
+    tc_gemm(a, b, c, "gelu")
+    x = b[0, :, 0].float()
+    ref = F.gelu(x)
+    torch.testing.assert_close(c[0, 0].float(), ref.to(torch.bfloat16).float(), rtol=0, atol=1e-2)
+    r = x.to(torch.bfloat16).expand(1, M, N).contiguous()
+    ones = torch.zeros(1, N, K, device="cuda")
+    ones[0, :, 0] = 1.0
+    tc_gemm(a, ones.to(torch.bfloat16), c, "dgelu", R=r)
+    xg = x.clone().requires_grad_(True)
+    F.gelu(xg).backward(torch.ones_like(xg))
+    torch.testing.assert_close(c[0, 0].float(), xg.grad.to(torch.bfloat16).float(), rtol=0, atol=1e-2)
