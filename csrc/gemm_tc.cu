@@ -34,7 +34,7 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kEpiWarps = 8;   // two warps per TMEM lane quarter, splitting the columns
+constexpr int kEpiWarps = 12;  // three warps per TMEM lane quarter, splitting the columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
@@ -263,15 +263,42 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
   } else {
     // ---------------- epilogue ----------------
-    const int ew = warp - 2;                    // epilogue warp 0..7
-    const int q = warp & 3;                     // TMEM lane quarter this warp may access
-    const int half = ew >> 2;                   // which half of the columns
+    // Warp ew owns TMEM lane quarter q (rows q*32..q*32+31 of the tile) and the
+    // 32-column chunks c with (c / 32) % 3 == part.  Per chunk: stage the
+    // residual / pre-activation block (prefetched into registers one chunk
+    // ahead), tcgen05.ld the accumulator, apply the epilogue, stage bf16 rows
+    // in swizzled smem and store them as coalesced 64-byte row segments.
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int part = ew >> 2;
+    constexpr int kParts = kEpiWarps / 4;
     uint8_t* stC = stage_base + ew * 2 * 2048;
     uint8_t* stR = stC + 2048;
     uint8_t* stX = stR;   // GELU (AUX) and residual/dGELU (R) never occur together
-    // lane -> (row, 16-byte chunk) for the cooperative, coalesced row copies
     const int cr = lane >> 2, cc = lane & 3;
     auto sw = [](int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); };
+    const bool has_r = (p.epi == kResidual || p.epi == kDGelu);
+    // work items: (tile, chunk) in this warp's order
+    auto first_chunk = [&]() { return part * 32; };
+    auto next_work = [&](int& t, int& c) {
+      c += kParts * 32;
+      if (c >= BN) { c = first_chunk(); t += gridDim.x; }
+    };
+    auto load_r = [&](int t, int c, uint4* dst) {
+      int l, mb, nb;
+      tile_coords(p, t, l, mb, nb);
+      const int m0 = mb * BM + q * 32;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = cr + 8 * i;
+        dst[i] = (m0 + r < p.M)
+                     ? __ldcs(reinterpret_cast<const uint4*>(p.R + l * p.r_ls + int64_t(m0 + r) * p.r_ms + nb * BN + c +
+                                                             cc * 8))
+                     : make_uint4(0, 0, 0, 0);
+      }
+    };
+    uint4 pref[4];
+    if (has_r && first_chunk() < BN && blockIdx.x < p.tiles) load_r(blockIdx.x, first_chunk(), pref);
     int local = 0;
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++local) {
       const int a = local & 1;
@@ -279,21 +306,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       tc_fence_after();
       int l, mb, nb;
       tile_coords(p, t, l, mb, nb);
-      const int m0 = mb * BM + q * 32;          // first row of this warp's 32-row slab
+      const int m0 = mb * BM + q * 32;
       const int n0 = nb * BN;
 #pragma unroll 1
-      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
-        // residual / pre-activation block -> smem (coalesced 64-byte rows)
-        if (p.epi == kResidual || p.epi == kDGelu) {
+      for (int c = first_chunk(); c < BN; c += kParts * 32) {
+        if (has_r) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int r = cr + 8 * i;
-            uint4 val = make_uint4(0, 0, 0, 0);
-            if (m0 + r < p.M)
-              val = *reinterpret_cast<const uint4*>(p.R + l * p.r_ls + int64_t(m0 + r) * p.r_ms + n0 + c + cc * 8);
-            *reinterpret_cast<uint4*>(stR + sw(r, cc)) = val;
-          }
+          for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(stR + sw(cr + 8 * i, cc)) = pref[i];
           __syncwarp();
+          int tn = t, cn = c;
+          next_work(tn, cn);
+          if (tn < p.tiles) load_r(tn, cn, pref);   // in flight during this chunk
         }
         float v[32];
         tc_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(a * BN + c), v);
@@ -313,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (p.epi == kGelu) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu_f(__bfloat162float(__float2bfloat16_rn(v[j])));
-        } else if (p.epi == kResidual || p.epi == kDGelu) {
+        } else if (has_r) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint4 pk = *reinterpret_cast<const uint4*>(stR + sw(lane, j));
@@ -338,16 +361,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           *reinterpret_cast<uint4*>(stC + sw(lane, j)) = pk;
         }
         __syncwarp();
-        // coalesced stores: 4 lanes cover one 64-byte row segment, 8 rows per pass
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int r = cr + 8 * i;
           if (m0 + r < p.M) {
-            *reinterpret_cast<uint4*>(p.C + l * p.c_ls + int64_t(m0 + r) * p.c_ms + n0 + c + cc * 8) =
-                *reinterpret_cast<const uint4*>(stC + sw(r, cc));
+            __stcs(reinterpret_cast<uint4*>(p.C + l * p.c_ls + int64_t(m0 + r) * p.c_ms + n0 + c + cc * 8),
+                   *reinterpret_cast<const uint4*>(stC + sw(r, cc)));
             if (p.epi == kGelu && p.AUX)
-              *reinterpret_cast<uint4*>(p.AUX + l * p.aux_ls + int64_t(m0 + r) * p.aux_ms + n0 + c + cc * 8) =
-                  *reinterpret_cast<const uint4*>(stX + sw(r, cc));
+              __stcs(reinterpret_cast<uint4*>(p.AUX + l * p.aux_ls + int64_t(m0 + r) * p.aux_ms + n0 + c + cc * 8),
+                     *reinterpret_cast<const uint4*>(stX + sw(r, cc)));
           }
         }
         __syncwarp();
@@ -464,9 +486,9 @@ void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optiona
   const CUtensorMap ta = make_map(A.data_ptr(), K, M, L, A.stride(1), A.stride(0), tc::BM, p.a_mode);
   const CUtensorMap tb = make_map(B.data_ptr(), K, N, B.size(0), B.stride(1), B.stride(0), BN, p.b_mode);
   p.b_shared = (B.size(0) == 1) ? 1 : 0;
-  if (BN == 256) launch<256, 4>(ta, tb, p);
-  else if (BN == 128) launch<128, 6>(ta, tb, p);
-  else launch<64, 8>(ta, tb, p);
+  if (BN == 256) launch<256, 3>(ta, tb, p);
+  else if (BN == 128) launch<128, 4>(ta, tb, p);
+  else launch<64, 6>(ta, tb, p);
 }
 
 }  // namespace pd
