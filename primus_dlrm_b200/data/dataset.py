@@ -371,14 +371,20 @@ def collate_to_dict(samples: list[dict]) -> dict[str, torch.Tensor]:
 
 
 class _CandidateMixin:
-    """Device batches for candidate scoring (shared by the real and synthetic eval sets)."""
+    """Device batches for candidate scoring (shared by the real and synthetic eval sets).
+
+    A counter block is emitted whenever the model consumes it (the config
+    declares that dense feature), zero-filled when the data has no counters."""
+
+    def _wants(self, name: str) -> bool:
+        return any(d.name == name for d in self.config.feature.dense_features)
 
     def user_batch(self, sample: dict, device) -> dict[str, torch.Tensor]:
         h = sample["history"]
         out = {f"hist_{p}_{k}_ids": torch.from_numpy(np.asarray(h[f"{p}_{k}s"])).long().unsqueeze(0).to(device)
                for p in POOLS for k in ("item", "artist", "album")}
         out["uid"] = torch.tensor([sample["uid"]], dtype=torch.long, device=device)
-        if self.config.data.enable_counters:
+        if self._wants("user_counters"):
             out["user_counters"] = torch.from_numpy(self.get_user_counters(sample["uid"])).float().unsqueeze(0).to(device)
         return out
 
@@ -388,13 +394,13 @@ class _CandidateMixin:
                "artist_id": torch.from_numpy(self.item_to_artist[items]).to(device),
                "album_id": torch.from_numpy(self.item_to_album[items]).to(device),
                "audio_embed": torch.from_numpy(self.audio_embeddings[items]).float().to(device)}
-        if self.config.data.enable_counters:
+        if self._wants("item_counters"):
             out["item_counters"] = torch.from_numpy(self.get_item_counters_batch(items)).float().to(device)
         return out
 
     def with_user_features(self, cand: dict, sample: dict, items, device) -> dict[str, torch.Tensor]:
         out = dict(cand)
-        if self.config.data.enable_counters:
+        if self._wants("cross_counters"):
             out["cross_counters"] = torch.from_numpy(
                 self.get_cross_counters_batch(sample["uid"], np.asarray(items, np.int64))).float().to(device)
         return out

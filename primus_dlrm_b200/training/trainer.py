@@ -206,7 +206,7 @@ class DistributedTrainer:
                         tfl = self.flops_per_sample * wthr / world / 1e12 if self.flops_per_sample else 0.0
                         mfu = 100 * tfl * 1e12 / peak if peak else 0.0
                         lr = self.engine.optimizer.param_groups[0]["lr"]
-                        tl = " | ".join(f"{k}={float(v):.4f}" for k, v in task_losses.items())
+                        tl = " | ".join(f"{k}={float(v.detach()):.4f}" for k, v in task_losses.items())
                         logger.info(f"epoch={epoch} step={step} | loss={lv:.4f} | lr={lr:.6f} | "
                                     f"global_throughput={thr:.0f} samples/s | window_throughput={wthr:.0f} "
                                     f"samples/s (over {self.log_interval} steps) | {tl} | tflops/gpu={tfl:.1f} "
