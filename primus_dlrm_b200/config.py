@@ -302,6 +302,10 @@ class TrainConfig:
     nan_guard: bool = False
     # host watchdog: seconds a step may take before the trainer raises (0 = off)
     step_timeout_s: float = 0.0
+    # peer heartbeats in the process group's store: a peer silent for this
+    # many seconds (or one that reported a failure) stops the others between
+    # steps with PeerFailure (0 = off)
+    heartbeat_timeout_s: float = 0.0
 
 
 @dataclass

@@ -15,6 +15,8 @@ single-GPU ``primus_dlrm/training/trainer.py``).
 * epoch-end checkpoint (rank-0 assembled, atomic) and evaluation;
 * a host watchdog that ends the process when a step does not finish within
   ``train.step_timeout_s`` (0 = off), so a dead peer surfaces as an error;
+* peer heartbeats (``parallel.health``): a rank that raised or went silent
+  stops the others between steps with ``PeerFailure``;
 * an optional NaN/Inf guard that skips the optimizer step.
 """
 from __future__ import annotations
@@ -30,6 +32,7 @@ import torch.distributed as dist
 
 from primus_dlrm_b200.config import Config
 from primus_dlrm_b200.data.batch import DeviceBatchStager, PackedBatch
+from primus_dlrm_b200.parallel.health import HealthMonitor
 from primus_dlrm_b200.parallel.setup import barrier, get_rank, get_world_size, is_main_process
 from primus_dlrm_b200.training.checkpoint import save_checkpoint
 from primus_dlrm_b200.training.engine import TrainEngine
@@ -78,13 +81,15 @@ def gather_max_gpu_memory(device) -> str:
 
 
 class Watchdog:
-    """Host thread: if ``kick()`` is not called for ``timeout_s`` seconds,
-    ``on_timeout`` runs (default: log and exit the process with code 17)."""
+    """Host thread: once armed by the first ``kick()`` (the first step may
+    include one-time setup), if ``kick()`` is not called again within
+    ``timeout_s`` seconds ``on_timeout`` runs (default: log and exit the
+    process with code 17)."""
 
     def __init__(self, timeout_s: float, on_timeout=None):
         self.timeout_s = timeout_s
         self.on_timeout = on_timeout or self._default
-        self._last = time.monotonic()
+        self._last = None
         self._stop = threading.Event()
         self.fired = False
         self._t = threading.Thread(target=self._run, daemon=True)
@@ -101,7 +106,8 @@ class Watchdog:
 
     def _run(self) -> None:
         while not self._stop.wait(min(1.0, self.timeout_s / 4)):
-            if time.monotonic() - self._last > self.timeout_s:
+            last = self._last
+            if last is not None and time.monotonic() - last > self.timeout_s:
                 self.fired = True
                 self.on_timeout()
                 return
@@ -134,6 +140,7 @@ class DistributedTrainer:
             self.tracer = Tracer(self.run_dir / "trace", trace_steps=trace_steps, warmup=trace_warmup,
                                  active=trace_active, rank=get_rank())
         self.watchdog = Watchdog(config.train.step_timeout_s)
+        self.health = HealthMonitor(config.train.heartbeat_timeout_s)
         if is_main_process():
             log_param_summary(model, config, get_world_size())
             if self.flops_per_sample:
@@ -170,6 +177,16 @@ class DistributedTrainer:
             yield stager.get()
 
     def train(self) -> dict:
+        try:
+            return self._train()
+        except BaseException as e:
+            self.health.report_failure(f"{type(e).__name__}: {e}")
+            self.watchdog.stop()
+            raise
+        finally:
+            self.health.stop()
+
+    def _train(self) -> dict:
         tc = self.config.train
         world = get_world_size()
         per_gpu = tc.batch_size // max(world, 1)
@@ -186,7 +203,9 @@ class DistributedTrainer:
             n = 0
             epoch_loss = torch.zeros((), device=self.device)
             for batch in self._device_batches():
+                self.health.check()          # a failed peer stops us before this step's launches
                 loss, task_losses = self.engine.step(batch)
+                self.health.beat(self.engine.global_step)
                 self.watchdog.kick()
                 if self.tracer:
                     self.tracer.step()

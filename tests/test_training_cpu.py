@@ -205,6 +205,8 @@ def test_watchdog_fires_and_kicks():
     from primus_dlrm_b200.training.trainer import Watchdog
     fired = []
     w = Watchdog(0.4, on_timeout=lambda: fired.append(time.monotonic()))
+    time.sleep(0.8)              # not armed before the first kick
+    assert not fired
     for _ in range(4):           # kicked: never fires
         time.sleep(0.15)
         w.kick()
