@@ -1,0 +1,551 @@
+// Pyramid causal attention on the 5th-generation tensor cores (tcgen05 +
+// TMEM + TMA) for sm_100a.
+//
+// Semantics (primus_dlrm/models/onetrans.py:62-67,146-166): the queries are
+// the LAST q_len of the T tokens of a [B, T, 3, H, d] fused projection; query
+// i (absolute position p = T - q_len + i) attends keys j <= p; scale 1/sqrt(d).
+//
+// Forward, one CTA = one 128-query tile at a time (persistent over tiles, two
+// CTAs per SM so one CTA's softmax overlaps the other's matrix work):
+//   warp 0     TMA: the Q tile (double-buffered across items), then K_j / V_j
+//              tiles into a ring
+//   warp 1     TMEM owner + MMA issuer (one elected lane):
+//                S_j  = Q K_j^T            (SS: both operands in smem, K-major)
+//                O   += P_{j-1} V_{j-1}    (TS: P from TMEM, V in smem MN-major)
+//   warps 2-5  softmax: thread = query row = TMEM lane, so row max / sum need
+//              no shuffles; the 128-key row is read from TMEM twice (max,
+//              then exp) in 64-column halves. The running max is only raised
+//              when it grows by more than 2^8 (log2 domain), so O in TMEM is
+//              rescaled rarely.
+//              P (bf16) goes back to TMEM for the PV product; l and O use the
+//              same reference max, so a stale max is exact.
+// TMEM (256 columns): S [0,128) fp32, O [128, 128+d) fp32, P [128+d, 128+2d)
+// as packed bf16 pairs (64 columns for a 128-key row).
+//
+// Every wait is bounded (2 s on %globaltimer); on timeout the error word
+// gets kWaitTimeout, the roles leave their loops, drain their own in-flight
+// copies / MMAs (bounded) and the CTA frees TMEM and exits.
+#include "common.cuh"
+
+#include <cuda.h>
+
+namespace pd {
+namespace atc {
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr int kTile = 128;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err) {
+  if (mbar_try(b, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try(b, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_error(err, kWaitTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+// 5-D tiled TMA load (no multicast) completing on an mbarrier.
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], "
+      "[%2];" ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(smem_u32(bar)) : "memory");
+}
+// D (tmem) (+)= A (smem desc) * B (smem desc)
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d), "l"(da), "l"(db), "r"(idesc), "r"(acc) : "memory");
+}
+// D (tmem) (+)= A (tmem, K-major packed bf16 pairs) * B (smem desc)
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d), "r"(a_tmem), "l"(db), "r"(idesc), "r"(acc) : "memory");
+}
+// 32 lanes x 32 consecutive 32-bit columns: thread = lane, r[i] = column i.
+__device__ __forceinline__ void tm_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tm_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// wait::ld that also names the 32 destination registers, so no use of them
+// can be scheduled before the wait.
+__device__ __forceinline__ void tm_ld_wait(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :: "memory");
+}
+__device__ __forceinline__ void tm_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+        "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tm_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tm_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// 2^x on the FMA/ALU pipes, used for a quarter of the exponentials so the
+// MUFU unit (16 ex2 per clock per SM) is not the only one working: Cody-Waite
+// style reduction x = n + f with n = round(x) via the 1.5 * 2^23 shifter and
+// f in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients were
+// fitted here (iteratively reweighted least squares on Chebyshev nodes,
+// max relative error 7.5e-5, well below the bf16 rounding of P); 2^n is
+// added to the exponent field. Inputs below -125 return ~2^-125.
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.055179596f, f, 0.24261186f), f, 0.69325954f), f, 0.99992800f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Shared-memory operand geometry for [rows][d] bf16 tiles as written by TMA
+// with the d-wide swizzle: rows of 2d bytes, 8-row atoms (SWIZZLE_64B for
+// d = 32, SWIZZLE_128B for d = 64).
+template <int D>
+struct Geo {
+  static constexpr int RB = D * 2;                   // bytes per row
+  static constexpr int kTileBytes = kTile * RB;      // one 128-row tile
+  static constexpr uint64_t kSwz = (D == 32) ? 4 : 2;  // descriptor layout code
+  static constexpr uint32_t kAtom = 8 * RB;          // bytes per 8-row atom
+};
+__device__ __forceinline__ uint64_t make_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint64_t swz) {
+  return uint64_t((addr >> 4) & 0x3FFF) | (uint64_t((lbo >> 4) & 0x3FFF) << 16) |
+         (uint64_t((sbo >> 4) & 0x3FFF) << 32) | (uint64_t(1) << 46) | (swz << 61);
+}
+// K-major operand (rows = M or N, d = K): k-step kk (16 elements) starts 32 B further.
+template <int D>
+__device__ __forceinline__ uint64_t desc_k(uint32_t tile, int kk) {
+  return make_desc(tile + uint32_t(kk) * 32u, 16u, Geo<D>::kAtom, Geo<D>::kSwz);
+}
+// MN-major operand (rows = K, d = M or N, one swizzle atom wide): k-step kk
+// covers rows [16 kk, 16 kk + 16), i.e. two 8-row atoms.
+template <int D>
+__device__ __forceinline__ uint64_t desc_mn(uint32_t tile, int kk) {
+  return make_desc(tile + uint32_t(kk) * 2u * Geo<D>::kAtom, uint32_t(Geo<D>::kTileBytes), Geo<D>::kAtom,
+                   Geo<D>::kSwz);
+}
+// kind::f16 instruction descriptor: f32 accumulate, bf16 A/B; majors per operand.
+__host__ __device__ constexpr uint32_t idesc(int m, int n, int a_mn, int b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
+         (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+struct FwdArgs {
+  int B, H, T, q_len, nq, items;
+  float c2;                 // softmax scale * log2(e)
+  __nv_bfloat16* o;         // [B, q_len, H, D]
+  float* lse;               // [B, H, q_len], log2 domain
+  int* err;
+};
+
+constexpr int kFwdThreads = 192;
+
+template <int D, int STAGES>
+__global__ void __launch_bounds__(kFwdThreads, 2) fmha_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm,
+                                                                     const FwdArgs a) {
+  using G = Geo<D>;
+  constexpr uint32_t kCols = 256;
+  constexpr uint32_t cS = 0, cO = 128, cP = 128 + D;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                                   // two Q buffers (next item's Q prefetched)
+  uint8_t* sK = sQ + 2 * G::kTileBytes;
+  uint8_t* sV = sK + STAGES * G::kTileBytes;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sV + STAGES * G::kTileBytes);
+  uint64_t* q_full = bar;       // [2]
+  uint64_t* q_empty = bar + 2;  // [2]
+  uint64_t* s_full = bar + 4;
+  uint64_t* p_full = bar + 5;
+  uint64_t* o_full = bar + 6;
+  uint64_t* o_free = bar + 7;
+  uint64_t* mma_done = bar + 8;
+  uint64_t* kv_full = bar + 9;
+  uint64_t* kv_empty = kv_full + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kv_empty + STAGES);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full[0], 1); mbar_init(&q_full[1], 1); mbar_init(&q_empty[0], 1); mbar_init(&q_empty[1], 1);
+    mbar_init(s_full, 1); mbar_init(p_full, 128);
+    mbar_init(o_full, 1); mbar_init(o_free, 128); mbar_init(mma_done, 1);
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tm) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(tmem_slot)), "r"(kCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int off = a.T - a.q_len;  // absolute position of query 0
+  // contiguous item range per CTA: whole (b, h) groups (equal cost) and the
+  // K / V tiles of a head reused from L2 by consecutive items
+  const int per = (a.items + gridDim.x - 1) / gridDim.x;
+  const int w_begin = blockIdx.x * per;
+  const int w_end = min(a.items, w_begin + per);
+
+  auto decode = [&](int w, int& b, int& h, int& i0, int& nkv) {
+    const int bh = w / a.nq;
+    i0 = (w - bh * a.nq) * kTile;
+    b = bh / a.H;
+    h = bh - b * a.H;
+    const int last = min(a.T - 1, off + i0 + kTile - 1);
+    nkv = last / kTile + 1;
+  };
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int kv_cnt = 0, item = 0;
+      int issued_q[2] = {0, 0}, issued_kv[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) issued_kv[s] = 0;
+      for (int w = w_begin; w < w_end && !*abort_flag; ++w, ++item) {
+        int b, h, i0, nkv;
+        decode(w, b, h, i0, nkv);
+        const int qb = item & 1;
+        if (!mbar_wait(&q_empty[qb], ((item >> 1) & 1) ^ 1, a.err)) { *abort_flag = 1; break; }
+        mbar_expect_tx(&q_full[qb], G::kTileBytes);
+        tma_load_5d(sQ + qb * G::kTileBytes, &tm, &q_full[qb], 0, h, 0, off + i0, b);
+        ++issued_q[qb];
+        for (int j = 0; j < nkv; ++j, ++kv_cnt) {
+          const int st = kv_cnt % STAGES, n = kv_cnt / STAGES;
+          if (!mbar_wait(&kv_empty[st], (n & 1) ^ 1, a.err)) { *abort_flag = 1; break; }
+          mbar_expect_tx(&kv_full[st], 2 * G::kTileBytes);
+          tma_load_5d(sK + st * G::kTileBytes, &tm, &kv_full[st], 0, h, 1, j * kTile, b);
+          tma_load_5d(sV + st * G::kTileBytes, &tm, &kv_full[st], 0, h, 2, j * kTile, b);
+          ++issued_kv[st];
+        }
+      }
+      if (*abort_flag) {  // every issued copy lands before the CTA may exit
+        for (int qb = 0; qb < 2; ++qb)
+          if (issued_q[qb] > 0) (void)mbar_wait(&q_full[qb], uint32_t(issued_q[qb] - 1) & 1u, a.err);
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s)
+          if (issued_kv[s] > 0) (void)mbar_wait(&kv_full[s], uint32_t(issued_kv[s] - 1) & 1u, a.err);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc(128, 128, 0, 0);
+      constexpr uint32_t id_pv = idesc(128, D, 0, 1);
+      int kv_cnt = 0, tile = 0, item = 0;
+      for (int w = w_begin; w < w_end && !*abort_flag; ++w, ++item) {
+        int b, h, i0, nkv;
+        decode(w, b, h, i0, nkv);
+        const int qb = item & 1;
+        if (!mbar_wait(&q_full[qb], (item >> 1) & 1, a.err)) { *abort_flag = 1; break; }
+        tc_fence_after();
+        int prev_st = 0;
+        bool ok = true;
+        for (int j = 0; j <= nkv; ++j) {
+          int st = 0;
+          if (j < nkv) {
+            st = kv_cnt % STAGES;
+            if (!mbar_wait(&kv_full[st], (kv_cnt / STAGES) & 1, a.err)) { ok = false; break; }
+            tc_fence_after();
+          }
+          if (j > 0) {
+            // O += P_{j-1} V_{j-1}
+            if (!mbar_wait(p_full, (tile - 1) & 1, a.err)) { ok = false; break; }
+            if (j == 1 && !mbar_wait(o_free, (item & 1) ^ 1, a.err)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t vt = smem_u32(sV + prev_st * G::kTileBytes);
+#pragma unroll
+            for (int kk = 0; kk < kTile / 16; ++kk)
+              mma_ts(tmem + cO, tmem + cP + uint32_t(kk * 8), desc_mn<D>(vt, kk), id_pv, (j > 1 || kk > 0) ? 1u : 0u);
+            tc_commit(&kv_empty[prev_st]);
+          }
+          if (j < nkv) {
+            // S_j = Q K_j^T
+            const uint32_t qt = smem_u32(sQ + qb * G::kTileBytes), kt = smem_u32(sK + st * G::kTileBytes);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+              mma_ss(tmem + cS, desc_k<D>(qt, kk), desc_k<D>(kt, kk), id_s, kk > 0 ? 1u : 0u);
+            tc_commit(s_full);
+            if (j == nkv - 1) tc_commit(&q_empty[qb]);
+            prev_st = st;
+            ++kv_cnt;
+            ++tile;
+          }
+        }
+        if (!ok) { *abort_flag = 1; break; }
+        tc_commit(o_full);
+      }
+      tc_commit(mma_done);
+      (void)mbar_wait(mma_done, 0, a.err);
+    }
+  } else {
+    // ---------------- softmax + epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;                      // row of the tile = TMEM lane
+    const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+    int tile = 0, item = 0;
+    for (int w = w_begin; w < w_end && !*abort_flag; ++w, ++item) {
+      int b, h, i0, nkv;
+      decode(w, b, h, i0, nkv);
+      const int p_abs = off + i0 + r;                       // this row's last visible key
+      float m = -1e30f, l = 0.f;
+      bool ok = true;
+      for (int j = 0; j < nkv; ++j, ++tile) {
+        if (!mbar_wait(s_full, tile & 1, a.err)) { ok = false; break; }
+        tc_fence_after();
+        const int lim = p_abs - j * kTile;                  // keys c <= lim are visible
+        const bool diag = __any_sync(0xffffffffu, lim < kTile - 1);   // warp-uniform masking
+        // pass 1: row max (8 independent partial maxima)
+        float mx8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
+#pragma unroll
+        for (int h0 = 0; h0 < kTile; h0 += 64) {
+          uint32_t sr[64];
+          tm_ld32(lane_base + cS + h0, sr);
+          tm_ld32(lane_base + cS + h0 + 32, sr + 32);
+          tm_ld_wait();
+          if (diag) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+              mx8[c & 7] = fmaxf(mx8[c & 7], (h0 + c <= lim) ? __uint_as_float(sr[c]) : -INFINITY);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sr[c]));
+          }
+        }
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        const float m_new = fmaxf(m, mx * a.c2);
+        const bool need = m_new > m + 8.0f;
+        if (__any_sync(0xffffffffu, need && j > 0)) {
+          // rescale O (quiescent: every earlier PV product completed before S_j)
+          const float alpha = need ? ex2(m - m_new) : 1.f;
+#pragma unroll
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            uint32_t orr[32];
+            tm_ld32(lane_base + cO + c0, orr);
+            tm_ld_wait();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) orr[c] = __float_as_uint(__uint_as_float(orr[c]) * alpha);
+            tm_st32(lane_base + cO + c0, orr);
+          }
+        }
+        if (need) {
+          l *= ex2(m - m_new);
+          m = m_new;
+        }
+        // pass 2: P = exp2(S c - m) -> bf16 pairs in TMEM (8 independent partial sums)
+        float sm8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sm8[e] = 0.f;
+#pragma unroll
+        for (int h0 = 0; h0 < kTile; h0 += 64) {
+          uint32_t sr[64];
+          tm_ld32(lane_base + cS + h0, sr);
+          tm_ld32(lane_base + cS + h0 + 32, sr + 32);
+          tm_ld_wait();
+#pragma unroll
+          for (int q0 = 0; q0 < 64; q0 += 32) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int c = 0; c < 32; c += 2) {
+              const int k0 = h0 + q0 + c;
+              const float x0 = fmaf(__uint_as_float(sr[q0 + c]), a.c2, -m);
+              const float x1 = fmaf(__uint_as_float(sr[q0 + c + 1]), a.c2, -m);
+              float p0 = (c >= 24) ? ex2_poly(x0) : ex2(x0);   // columns 24..31 of each 32 on the FMA pipe
+              float p1 = (c >= 24) ? ex2_poly(x1) : ex2(x1);
+              if (diag) {
+                p0 = (k0 <= lim) ? p0 : 0.f;
+                p1 = (k0 + 1 <= lim) ? p1 : 0.f;
+              }
+              sm8[(c >> 1) & 7] += p0 + p1;
+              pk[c >> 1] = pack_bf16(p0, p1);
+            }
+            tm_st16(lane_base + cP + uint32_t((h0 + q0) >> 1), pk);
+          }
+        }
+        const float sum = ((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7]));
+        l += sum;
+        tm_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_full);
+      }
+      if (!ok || !mbar_wait(o_full, item & 1, a.err)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      const int qi = i0 + r;
+      const float inv = 1.f / l;
+      __nv_bfloat16* dst = a.o + ((int64_t(b) * a.q_len + qi) * a.H + h) * D;
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t orr[32];
+        tm_ld32(lane_base + cO + c0, orr);
+        tm_ld_wait();
+        if (qi < a.q_len) {
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            uint4 v;
+            v.x = pack_bf16(__uint_as_float(orr[c]) * inv, __uint_as_float(orr[c + 1]) * inv);
+            v.y = pack_bf16(__uint_as_float(orr[c + 2]) * inv, __uint_as_float(orr[c + 3]) * inv);
+            v.z = pack_bf16(__uint_as_float(orr[c + 4]) * inv, __uint_as_float(orr[c + 5]) * inv);
+            v.w = pack_bf16(__uint_as_float(orr[c + 6]) * inv, __uint_as_float(orr[c + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + c0 + c) = v;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(o_free);
+      if (qi < a.q_len) a.lse[(int64_t(b) * a.H + h) * a.q_len + qi] = m + __log2f(l);
+    }
+  }
+  // teardown: every role is out of its loop (all waits above are bounded)
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+  }
+}
+
+}  // namespace atc
+
+// ---------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------
+namespace {
+
+// 5-D map over a contiguous [B, T, 3, H, D] bf16 buffer; box = 128 rows of one
+// (b, part, head), swizzled by the row width (64 B for d = 32, 128 B for d = 64).
+CUtensorMap qkv_map(const at::Tensor& qkv) {
+  const int64_t B = qkv.size(0), T = qkv.size(1), H = qkv.size(3), D = qkv.size(4);
+  CUtensorMap m;
+  cuuint64_t dims[5] = {cuuint64_t(D), cuuint64_t(H), 3, cuuint64_t(T), cuuint64_t(B)};
+  cuuint64_t strides[4] = {cuuint64_t(D * 2), cuuint64_t(H * D * 2), cuuint64_t(3 * H * D * 2),
+                           cuuint64_t(T * 3 * H * D * 2)};
+  cuuint32_t box[5] = {cuuint32_t(D), 1, 1, cuuint32_t(atc::kTile), 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = cuTensorMapEncodeTiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, qkv.data_ptr(), dims, strides, box,
+                                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                      D == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled(qkv) failed: ", int(r));
+  return m;
+}
+
+void check_qkv5(const at::Tensor& qkv) {
+  TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 5 && qkv.is_contiguous(),
+              "qkv must be a contiguous bf16 [B, T, 3, H, d] CUDA tensor");
+  TORCH_CHECK(qkv.size(2) == 3 && (qkv.size(4) == 32 || qkv.size(4) == 64), "qkv: [B, T, 3, H, d] with d in {32, 64}");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16 == 0, "qkv must be 16-byte aligned");
+}
+
+template <int D, int STAGES>
+void launch_fwd(const CUtensorMap& tm, const atc::FwdArgs& a) {
+  constexpr size_t used = 1024 + (2 + 2 * STAGES) * atc::Geo<D>::kTileBytes + 256;
+  // at least 80 KB, so at most two CTAs (two 256-column TMEM allocations) share an SM
+  constexpr size_t smem = used > 81920 ? used : 81920;
+  static bool attr = false;
+  if (!attr) {
+    PD_CHECK_CUDA(cudaFuncSetAttribute(atc::fmha_fwd_tc_kernel<D, STAGES>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    attr = true;
+  }
+  const int grid = a.items < 2 * num_sms() ? a.items : 2 * num_sms();
+  atc::fmha_fwd_tc_kernel<D, STAGES><<<grid, atc::kFwdThreads, smem, stream()>>>(tm, a);
+  PD_CHECK_LAUNCH();
+}
+
+}  // namespace
+
+// qkv [B, T, 3, H, d] (contiguous) -> (o [B, q_len, H, d], lse [B, H, q_len] log2 domain)
+std::vector<at::Tensor> fmha_fwd_tc(at::Tensor qkv, int64_t q_len, double scale, at::Tensor err) {
+  check_qkv5(qkv);
+  const int B = int(qkv.size(0)), T = int(qkv.size(1)), H = int(qkv.size(3)), D = int(qkv.size(4));
+  TORCH_CHECK(q_len >= 1 && q_len <= T, "q_len must be in [1, T]");
+  auto o = at::empty({B, int64_t(q_len), H, D}, qkv.options());
+  auto lse = at::empty({B, H, int64_t(q_len)}, qkv.options().dtype(at::kFloat));
+  if (B == 0) return {o, lse};
+  atc::FwdArgs a{};
+  a.B = B; a.H = H; a.T = T; a.q_len = int(q_len);
+  a.nq = int((q_len + atc::kTile - 1) / atc::kTile);
+  a.items = B * H * a.nq;
+  a.c2 = float(scale * 1.4426950408889634);
+  a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  a.lse = lse.data_ptr<float>();
+  a.err = err.data_ptr<int>();
+  const CUtensorMap tm = qkv_map(qkv);
+  if (D == 32) launch_fwd<32, 3>(tm, a);
+  else launch_fwd<64, 2>(tm, a);
+  return {o, lse};
+}
+
+}  // namespace pd

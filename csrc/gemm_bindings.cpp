@@ -7,6 +7,7 @@ std::vector<at::Tensor> fmha_fwd(at::Tensor, at::Tensor, at::Tensor, double);
 void fmha_bwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor,
               at::Tensor, double);
 long long launches();
+std::vector<at::Tensor> fmha_fwd_tc(at::Tensor, int64_t, double, at::Tensor);
 void tc_gemm(at::Tensor, at::Tensor, at::Tensor, int64_t, c10::optional<at::Tensor>, c10::optional<at::Tensor>,
              at::Tensor);
 }  // namespace pd
@@ -14,6 +15,7 @@ void tc_gemm(at::Tensor, at::Tensor, at::Tensor, int64_t, c10::optional<at::Tens
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "primus_dlrm_b200 sm_100a tensor-core kernels";
   m.def("fmha_fwd", &pd::fmha_fwd, "pyramid causal attention forward -> (o, lse)");
+  m.def("fmha_fwd_tc", &pd::fmha_fwd_tc, "tcgen05 pyramid causal attention forward from qkv [B,T,3,H,d] -> (o, lse)");
   m.def("fmha_bwd", &pd::fmha_bwd, "pyramid causal attention backward into dq/dk/dv views");
   m.def("tc_gemm", &pd::tc_gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("epi") = 0,
         py::arg("R") = py::none(), py::arg("AUX") = py::none(), py::arg("err"),

@@ -16,6 +16,8 @@ Paths:
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.nn.functional as F
 
@@ -57,6 +59,32 @@ class _NativeFMHA(torch.autograd.Function):
         return buf[:, kl - ql:, 0], buf[:, :, 1], buf[:, :, 2], None
 
 
+def _tc_fwd_ok(qkv: torch.Tensor) -> bool:
+    """The tcgen05 forward reads qkv through one TMA map: contiguous, d in {32, 64}.
+    Opt-in (PD_ATTN_TC_FWD=1): on the v6 shapes it measures level with the
+    mma.sync forward, which therefore stays the default."""
+    g = _ext.gemm()
+    return (hasattr(g, "fmha_fwd_tc") and qkv.is_contiguous() and qkv.shape[-1] in (32, 64)
+            and os.environ.get("PD_ATTN_TC_FWD", "0") == "1")
+
+
+def _err_word(device) -> torch.Tensor:
+    w = _ERR.get(device)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=device)
+        _ERR[device] = w
+    return w
+
+
+_ERR: dict = {}
+
+
+def attention_error_code(device) -> int:
+    """Error word of the tcgen05 attention kernels (0 = ok, 2 = a bounded wait ran out)."""
+    w = _ERR.get(torch.device(device))
+    return int(w.item()) if w is not None else 0
+
+
 class _NativeFMHAFused(torch.autograd.Function):
     """Attention straight from the fused projection output qkv [B, T, 3, H, d]:
     queries are the last q_len rows; the gradient is one [B, T, 3, H, d]
@@ -67,7 +95,10 @@ class _NativeFMHAFused(torch.autograd.Function):
         G = _ext.gemm()
         T = qkv.shape[1]
         q, k, v = qkv[:, T - q_len:, 0], qkv[:, :, 1], qkv[:, :, 2]
-        o, lse = G.fmha_fwd(q, k, v, scale)
+        if _tc_fwd_ok(qkv):
+            o, lse = G.fmha_fwd_tc(qkv, q_len, scale, _err_word(qkv.device))
+        else:
+            o, lse = G.fmha_fwd(q, k, v, scale)
         ctx.scale, ctx.q_len = scale, q_len
         ctx.save_for_backward(qkv, o, lse)
         return o

@@ -50,3 +50,54 @@ def test_fmha_layout_strided_views():
     o = _NativeFMHA.apply(q, k, v, d ** -0.5)
     r = _ref(q.float(), k.float(), v.float())
     torch.testing.assert_close(o.float(), r, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("d", [32, 64])
+@pytest.mark.parametrize("ql,kl", [(912, 912), (786, 912), (32, 158), (1, 70), (200, 200), (130, 257), (129, 129)])
+def test_fmha_tc_fwd_matches_reference(d, ql, kl):
+    """tcgen05 forward (TMA + TMEM) vs fp32 attention; LSE in the log2 domain."""
+    from primus_dlrm_b200.ops import _ext
+    G = _ext.gemm()
+    torch.manual_seed(ql + 3 * kl + d)
+    B, H = 3, 4
+    qkv = (2.0 * torch.randn(B, kl, 3, H, d, device="cuda")).to(torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    o, lse = G.fmha_fwd_tc(qkv, ql, d ** -0.5, err)
+    x = qkv.float()
+    r = _ref(x[:, kl - ql:, 0], x[:, :, 1], x[:, :, 2])
+    assert int(err.item()) == 0
+    torch.testing.assert_close(o.float(), r, rtol=2e-2, atol=2e-2)
+    q, k = x[:, kl - ql:, 0], x[:, :, 1]
+    s = torch.einsum("bqhd,bkhd->bhqk", q, k) / math.sqrt(d)
+    qi = torch.arange(ql, device="cuda")[:, None] + (kl - ql)
+    s = s.masked_fill(torch.arange(kl, device="cuda")[None, :] > qi, float("-inf"))
+    lse_ref = torch.logsumexp(s, -1) / math.log(2.0)
+    torch.testing.assert_close(lse, lse_ref, rtol=1e-3, atol=1e-2)
+
+
+def test_fmha_tc_large_logits_rescale():
+    """Rows whose running max grows across key tiles exercise the O rescale."""
+    from primus_dlrm_b200.ops import _ext
+    G = _ext.gemm()
+    B, H, d, kl = 2, 2, 32, 400
+    torch.manual_seed(0)
+    qkv = torch.randn(B, kl, 3, H, d, device="cuda")
+    qkv[:, :, 1] *= torch.linspace(0.1, 6.0, kl, device="cuda")[None, :, None, None]   # growing logits
+    qkv = qkv.to(torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    o, _ = G.fmha_fwd_tc(qkv, kl, d ** -0.5, err)
+    x = qkv.float()
+    torch.testing.assert_close(o.float(), _ref(x[:, :, 0], x[:, :, 1], x[:, :, 2]), rtol=2e-2, atol=2e-2)
+
+
+def test_fmha_tc_fwd_vs_reference_pyramid_v6_shapes():
+    """Every layer shape of the v6 pyramid (d = 32, 8 heads), small batch."""
+    from primus_dlrm_b200.ops import _ext
+    G = _ext.gemm()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for ql, kl in [(912, 912), (661, 786), (409, 535), (158, 283), (32, 158)]:
+        qkv = torch.randn(2, kl, 3, 8, 32, device="cuda").to(torch.bfloat16)
+        o, _ = G.fmha_fwd_tc(qkv, ql, 32 ** -0.5, err)
+        x = qkv.float()
+        torch.testing.assert_close(o.float(), _ref(x[:, kl - ql:, 0], x[:, :, 1], x[:, :, 2]), rtol=2e-2, atol=2e-2)
+    assert int(err.item()) == 0
