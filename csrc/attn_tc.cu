@@ -47,13 +47,16 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
+// try_wait with a suspend-time hint: a waiting warp sleeps (issuing nothing)
+// until the phase completes or ~0.2 ms pass, instead of spinning and taking
+// issue slots from the warps that do the work.
 __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
+      : "=r"(ok) : "r"(smem_u32(b)), "r"(parity), "r"(200000u) : "memory");
   return ok != 0;
 }
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err) {
@@ -476,6 +479,441 @@ __global__ void __launch_bounds__(kFwdThreads, 2) fmha_fwd_tc_kernel(const __gri
   }
 }
 
+// ===========================================================================
+// Backward (d = 32): one persistent CTA per (b, h) at a time.
+//
+//   for each 128-key tile j (K_j, V_j double-buffered in smem)
+//     for each 128-query tile i that sees any key of j
+//       S^T  = K_j Q_i^T      dP^T = V_j dO_i^T           (SS MMAs -> TMEM)
+//       compute warps: P^T = exp2(S^T c - lse), dS^T = P^T (dP^T - delta)
+//       dV_j += P^T dO_i      dK_j += dS^T Q_i            (TS: A = P^T / dS^T in TMEM)
+//       dQ_i  = dS K_j                                     (SS: dS from a swizzled smem tile)
+//       compute warps add dQ_i into an fp32 dQ block in shared memory
+//   dQ, dK, dV are written once, in bf16, straight into the fused-QKV
+//   gradient; the Q rows the pyramid pruned get zeros.
+// One CTA owns every key tile of the head, so dQ accumulates in shared
+// memory (no fp32 atomics, no accumulator buffer, no conversion pass) and
+// delta = rowsum(dO * O) is computed in the CTA's prologue: one launch.
+// With d = 32 the dV / dK / dQ products are N = 32 MMAs, whose cost is
+// dominated by operand traffic; taking A from TMEM for dV and dK (thread =
+// key row writes P^T / dS^T straight into TMEM lanes) leaves only dQ reading
+// a 4 KB A operand from shared memory.
+//
+// Warps: 0 TMA, 1 TMEM + MMA issuer, 2..17 compute (warp w reads TMEM lanes
+// 32 (w % 4)..+31 = key rows; (w - 2) / 4 selects 32 of the 128 query columns).
+// TMEM (512 columns): S^T [0,128), dP^T [128,256), P^T bf16 [256,320),
+// dS^T bf16 [320,384), dV [384,416), dK [416,448), dQ [448,480).
+// The MMA warp issues the next pair's S^T / dP^T as soon as the compute
+// warps have read the current ones, so the exponentials of pair p + 1
+// overlap the dV / dK / dQ products of pair p.
+// ===========================================================================
+struct BwdArgs {
+  int B, H, T, q_len, nq, nkv, items;
+  float c2, scale;
+  const __nv_bfloat16* o;     // [B, q_len, H, 32]
+  const __nv_bfloat16* dout;  // [B, q_len, H, 32]
+  const float* lse;           // [B, H, q_len]
+  __nv_bfloat16* dqkv;        // [B, T, 3, H, 32]
+  int* err;
+  long long* dbg;             // optional per-stage clock stamps of CTA 0 (profiling aid), or null
+};
+
+constexpr int kBwdCompute = 16;                       // compute warps
+constexpr int kBwdThreads = 64 + 32 * kBwdCompute;
+constexpr int kBwdCT = 32 * kBwdCompute;              // compute threads
+constexpr int kDbgPairs = 64, kDbgSlots = 16;
+
+// Pair enumeration shared by every role: items (b, h) of this CTA, key tiles,
+// then the query tiles that see the key tile.
+struct PairIt {
+  int w, w_end, jt, i, first_i;
+  int off, nq, nkv;
+  __device__ void first_q() {
+    const int k0 = jt * kTile;
+    first_i = k0 > off ? (k0 - off) / kTile : 0;
+    i = first_i;
+  }
+  __device__ void start(const BwdArgs& a, int wb, int we) {
+    w = wb; w_end = we; off = a.T - a.q_len; nq = a.nq; nkv = a.nkv; jt = 0;
+    first_q();
+  }
+  __device__ bool valid() const { return w < w_end; }
+  __device__ bool last_of_kv() const { return i == nq - 1; }
+  __device__ bool first_of_kv() const { return i == first_i; }
+  __device__ void next() {
+    if (++i < nq) return;
+    if (++jt < nkv) { first_q(); return; }
+    ++w; jt = 0; first_q();
+  }
+};
+
+__device__ __forceinline__ void dbg_stamp(const BwdArgs& a, int pc, int slot) {
+  if (a.dbg != nullptr && blockIdx.x == 0 && pc < kDbgPairs) a.dbg[pc * kDbgSlots + slot] = clock64();
+}
+__device__ __forceinline__ void tm_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+__global__ void __launch_bounds__(kBwdThreads, 1) fmha_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                                                                    const __grid_constant__ CUtensorMap tm_do,
+                                                                    const BwdArgs a) {
+  constexpr int D = 32;
+  using G = Geo<D>;
+  constexpr uint32_t cS = 0, cdP = 128, cP = 256, cdS = 320, cdV = 384, cdK = 416, cdQ = 448;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;                                // [2] key tiles
+  uint8_t* sV = sK + 2 * G::kTileBytes;              // [2]
+  uint8_t* sQ = sV + 2 * G::kTileBytes;              // [2] stages
+  uint8_t* sdO = sQ + 2 * G::kTileBytes;             // [2] stages
+  uint8_t* sdS = sdO + 2 * G::kTileBytes;            // 128 x 128 bf16, MN-major SW128 for the dQ product
+  float* sLSE = reinterpret_cast<float*>(sdS + 32768);          // [nq * 128]
+  float* sDel = sLSE + a.nq * kTile;                             // [nq * 128]
+  float* sdQ = sDel + a.nq * kTile;                              // [q_len(8)] x 32 fp32, 16B chunks swizzled
+  const int qrows = (a.q_len + 7) & ~7;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sdQ + qrows * 32);
+  uint64_t* kv_full = bar;          // [2]
+  uint64_t* kv_empty = bar + 2;     // [2]
+  uint64_t* qd_full = bar + 4;      // [2]
+  uint64_t* qd_empty = bar + 6;     // [2]
+  uint64_t* s_full = bar + 8;
+  uint64_t* s_free = bar + 9;
+  uint64_t* p_full = bar + 10;
+  uint64_t* mma2_done = bar + 11;
+  uint64_t* mma_done = bar + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 13);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(&kv_full[k], 1); mbar_init(&kv_empty[k], 1); mbar_init(&qd_full[k], 1); mbar_init(&qd_empty[k], 1);
+    }
+    mbar_init(s_full, 1); mbar_init(s_free, kBwdCT); mbar_init(p_full, kBwdCT); mbar_init(mma2_done, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_qkv) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_do) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(tmem_slot)), "r"(512) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int per = (a.items + gridDim.x - 1) / gridDim.x;
+  const int w_begin = blockIdx.x * per, w_end = min(a.items, w_begin + per);
+  const int off = a.T - a.q_len;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      PairIt it;
+      it.start(a, w_begin, w_end);
+      int pc = 0, kc = 0;
+      int issued_kv[2] = {0, 0}, issued_qd[2] = {0, 0};
+      for (; it.valid() && !*abort_flag; it.next(), ++pc) {
+        const int b = it.w / a.H, h = it.w - (it.w / a.H) * a.H;
+        if (it.first_of_kv()) {
+          const int kb = kc & 1;
+          if (!mbar_wait(&kv_empty[kb], ((kc >> 1) & 1) ^ 1, a.err)) { *abort_flag = 1; break; }
+          mbar_expect_tx(&kv_full[kb], 2 * G::kTileBytes);
+          tma_load_5d(sK + kb * G::kTileBytes, &tm_qkv, &kv_full[kb], 0, h, 1, it.jt * kTile, b);
+          tma_load_5d(sV + kb * G::kTileBytes, &tm_qkv, &kv_full[kb], 0, h, 2, it.jt * kTile, b);
+          ++issued_kv[kb];
+          ++kc;
+        }
+        const int st = pc & 1;
+        if (!mbar_wait(&qd_empty[st], ((pc >> 1) & 1) ^ 1, a.err)) { *abort_flag = 1; break; }
+        mbar_expect_tx(&qd_full[st], 2 * G::kTileBytes);
+        tma_load_5d(sQ + st * G::kTileBytes, &tm_qkv, &qd_full[st], 0, h, 0, off + it.i * kTile, b);
+        asm volatile(
+            "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+            "[%2];" ::"r"(smem_u32(sdO + st * G::kTileBytes)), "l"(&tm_do), "r"(smem_u32(&qd_full[st])), "r"(0), "r"(h),
+            "r"(it.i * kTile), "r"(b) : "memory");
+        ++issued_qd[st];
+      }
+      if (*abort_flag) {
+        for (int k = 0; k < 2; ++k) {
+          if (issued_kv[k] > 0) (void)mbar_wait(&kv_full[k], uint32_t(issued_kv[k] - 1) & 1u, a.err);
+          if (issued_qd[k] > 0) (void)mbar_wait(&qd_full[k], uint32_t(issued_qd[k] - 1) & 1u, a.err);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc(128, 128, 0, 0);       // S^T, dP^T
+      constexpr uint32_t id_kv = idesc(128, D, 0, 1);        // dV, dK: A in TMEM, B (dO / Q) MN-major
+      constexpr uint32_t id_q = idesc(128, D, 1, 1);         // dQ: A (dS) MN-major, B (K) MN-major
+      PairIt cur;
+      cur.start(a, w_begin, w_end);
+      int pc = 0, kc = 0;          // pair index of `cur`, key tiles seen including cur's
+      bool ok = true;
+      auto issue_s = [&](const PairIt& it, int p, int& kcount) -> bool {
+        if (it.first_of_kv()) {
+          if (!mbar_wait(&kv_full[kcount & 1], (kcount >> 1) & 1, a.err)) return false;
+          ++kcount;
+        }
+        if (!mbar_wait(&qd_full[p & 1], (p >> 1) & 1, a.err)) return false;
+        tc_fence_after();
+        const int kb = (kcount - 1) & 1;
+        const uint32_t kt = smem_u32(sK + kb * G::kTileBytes), vt = smem_u32(sV + kb * G::kTileBytes);
+        const uint32_t qt = smem_u32(sQ + (p & 1) * G::kTileBytes), dt = smem_u32(sdO + (p & 1) * G::kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) mma_ss(tmem + cS, desc_k<D>(kt, kk), desc_k<D>(qt, kk), id_s, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) mma_ss(tmem + cdP, desc_k<D>(vt, kk), desc_k<D>(dt, kk), id_s, kk > 0);
+        tc_commit(s_full);
+        return true;
+      };
+      if (cur.valid()) ok = issue_s(cur, 0, kc);
+      while (ok && cur.valid() && !*abort_flag) {
+        const int kb = (kc - 1) & 1;
+        PairIt nxt = cur;
+        nxt.next();
+        int kc_next = kc;
+        if (nxt.valid()) {
+          if (!mbar_wait(s_free, pc & 1, a.err)) { ok = false; break; }
+          dbg_stamp(a, pc, 8);
+          tc_fence_after();
+          if (!issue_s(nxt, pc + 1, kc_next)) { ok = false; break; }
+          dbg_stamp(a, pc, 10);
+        }
+        if (!mbar_wait(p_full, pc & 1, a.err)) { ok = false; break; }
+        dbg_stamp(a, pc, 11);
+        tc_fence_after();
+        const uint32_t kt = smem_u32(sK + kb * G::kTileBytes);
+        const uint32_t qt = smem_u32(sQ + (pc & 1) * G::kTileBytes), dt = smem_u32(sdO + (pc & 1) * G::kTileBytes);
+        const uint32_t acc0 = cur.first_of_kv() ? 0u : 1u;
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          mma_ts(tmem + cdV, tmem + cP + uint32_t(8 * kk), desc_mn<D>(dt, kk), id_kv, (kk > 0) ? 1u : acc0);
+        dbg_stamp(a, pc, 14);
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          mma_ts(tmem + cdK, tmem + cdS + uint32_t(8 * kk), desc_mn<D>(qt, kk), id_kv, (kk > 0) ? 1u : acc0);
+        dbg_stamp(a, pc, 15);
+        const uint32_t ds = smem_u32(sdS);
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          mma_ss(tmem + cdQ, make_desc(ds + uint32_t(kk) * 2048u, 16384u, 1024u, 2), desc_mn<D>(kt, kk), id_q,
+                 kk > 0 ? 1u : 0u);
+        tc_commit(&qd_empty[pc & 1]);
+        if (cur.last_of_kv()) tc_commit(&kv_empty[kb]);
+        tc_commit(mma2_done);
+        dbg_stamp(a, pc, 12);
+        cur = nxt;
+        kc = kc_next;
+        ++pc;
+      }
+      if (!ok) *abort_flag = 1;
+      tc_commit(mma_done);
+      (void)mbar_wait(mma_done, 0, a.err);
+    }
+  } else {
+    // ---------------- compute warps ----------------
+    const int ct = threadIdx.x - 64;                   // 0 .. 511
+    const int quarter = warp & 3;
+    const int g = (warp - 2) >> 2;                     // query columns [32 g, 32 g + 32)
+    const int r = quarter * 32 + lane;                 // key row within the tile = TMEM lane
+    const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+    const bool stamp = (warp == 2 && lane == 0);
+    auto bar_compute = [&]() { asm volatile("bar.sync 1, %0;" ::"n"(kBwdCT) : "memory"); };
+    // dQ of a finished pair (lanes = query rows, this warp's 8 columns) into the smem block
+    auto add_dq = [&](int qi) {
+      uint32_t qr[8];
+      tm_ld8(lane_base + cdQ + uint32_t(8 * g), qr);
+      tm_ld_wait();
+      const int qrow = qi * kTile + r;
+      if (qrow < a.q_len) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int chunk = (2 * g + hh) ^ (qrow & 7);
+          float4* dst = reinterpret_cast<float4*>(sdQ + qrow * 32) + chunk;
+          float4 v = *dst;
+          v.x += __uint_as_float(qr[4 * hh]); v.y += __uint_as_float(qr[4 * hh + 1]);
+          v.z += __uint_as_float(qr[4 * hh + 2]); v.w += __uint_as_float(qr[4 * hh + 3]);
+          *dst = v;
+        }
+      }
+    };
+    // dK, dV of a finished key tile: lanes = key rows, this warp's 8 columns
+    auto write_dkv = [&](int b, int h, int jt) {
+      uint32_t kr[8], vr[8];
+      tm_ld8(lane_base + cdK + uint32_t(8 * g), kr);
+      tm_ld8(lane_base + cdV + uint32_t(8 * g), vr);
+      tm_ld_wait();
+      const int krow = jt * kTile + r;
+      if (krow < a.T) {
+        __nv_bfloat16* dk = a.dqkv + ((int64_t(b) * a.T + krow) * 3 + 1) * a.H * D + h * D + 8 * g;
+        __nv_bfloat16* dv = dk + a.H * D;
+        uint4 u, v;
+        u.x = pack_bf16(__uint_as_float(kr[0]) * a.scale, __uint_as_float(kr[1]) * a.scale);
+        u.y = pack_bf16(__uint_as_float(kr[2]) * a.scale, __uint_as_float(kr[3]) * a.scale);
+        u.z = pack_bf16(__uint_as_float(kr[4]) * a.scale, __uint_as_float(kr[5]) * a.scale);
+        u.w = pack_bf16(__uint_as_float(kr[6]) * a.scale, __uint_as_float(kr[7]) * a.scale);
+        v.x = pack_bf16(__uint_as_float(vr[0]), __uint_as_float(vr[1]));
+        v.y = pack_bf16(__uint_as_float(vr[2]), __uint_as_float(vr[3]));
+        v.z = pack_bf16(__uint_as_float(vr[4]), __uint_as_float(vr[5]));
+        v.w = pack_bf16(__uint_as_float(vr[6]), __uint_as_float(vr[7]));
+        *reinterpret_cast<uint4*>(dk) = u;
+        *reinterpret_cast<uint4*>(dv) = v;
+      }
+    };
+    PairIt it;
+    it.start(a, w_begin, w_end);
+    int pc = 0;
+    bool ok = true;
+    while (it.valid() && ok && !*abort_flag) {
+      const int w = it.w;
+      const int b = w / a.H, h = w - (w / a.H) * a.H;
+      // ---- prologue: lse, delta = rowsum(dO * O), zero dQ ----
+      for (int q = ct; q < a.nq * kTile; q += kBwdCT) {
+        float lse = INFINITY, del = 0.f;
+        if (q < a.q_len) {
+          lse = a.lse[(int64_t(b) * a.H + h) * a.q_len + q];
+          const int64_t base = ((int64_t(b) * a.q_len + q) * a.H + h) * D;
+          const uint4* po = reinterpret_cast<const uint4*>(a.o + base);
+          const uint4* pd = reinterpret_cast<const uint4*>(a.dout + base);
+#pragma unroll
+          for (int c = 0; c < D / 8; ++c) {
+            const uint4 u = po[c], v = pd[c];
+            const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&u);
+            const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 fx = __bfloat1622float2(x[e]), fy = __bfloat1622float2(y[e]);
+              del = fmaf(fx.x, fy.x, fmaf(fx.y, fy.y, del));
+            }
+          }
+        }
+        sLSE[q] = lse;
+        sDel[q] = del;
+      }
+      for (int k = ct; k < qrows * 8; k += kBwdCT) reinterpret_cast<float4*>(sdQ)[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      bar_compute();
+      int prev_i = -1, prev_jt = -1;
+      bool prev_last_kv = false;
+      for (; it.valid() && it.w == w; it.next(), ++pc) {
+        if (stamp) dbg_stamp(a, pc, 0);
+        if (!mbar_wait(s_full, pc & 1, a.err)) { ok = false; break; }
+        if (stamp) dbg_stamp(a, pc, 1);
+        tc_fence_after();
+        uint32_t sr[32], dr[32];
+        tm_ld32(lane_base + cS + uint32_t(32 * g), sr);
+        tm_ld32(lane_base + cdP + uint32_t(32 * g), dr);
+        tm_ld_wait();
+        tc_fence_before();
+        mbar_arrive(s_free);
+        if (stamp) dbg_stamp(a, pc, 2);
+        // P^T, dS^T for key row r, queries q0 + c
+        const int q0 = it.i * kTile + 32 * g;
+        const int key = it.jt * kTile + r;
+        const int lim = key - off - q0;                    // query column c is visible iff c >= lim
+        const int lim_hi = __reduce_max_sync(0xffffffffu, lim);
+        const int lim_lo = __reduce_min_sync(0xffffffffu, lim);
+        uint32_t pp[16], dd[16];
+        if (lim_lo > 31) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) { pp[c] = 0u; dd[c] = 0u; }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; c += 4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(sLSE + q0 + c);
+            const float4 d4 = *reinterpret_cast<const float4*>(sDel + q0 + c);
+            float p0 = ex2(fmaf(__uint_as_float(sr[c]), a.c2, -l4.x));
+            float p1 = ex2(fmaf(__uint_as_float(sr[c + 1]), a.c2, -l4.y));
+            float p2 = ex2(fmaf(__uint_as_float(sr[c + 2]), a.c2, -l4.z));
+            float p3 = ex2(fmaf(__uint_as_float(sr[c + 3]), a.c2, -l4.w));
+            if (lim_hi > 0) {
+              p0 = (c >= lim) ? p0 : 0.f;
+              p1 = (c + 1 >= lim) ? p1 : 0.f;
+              p2 = (c + 2 >= lim) ? p2 : 0.f;
+              p3 = (c + 3 >= lim) ? p3 : 0.f;
+            }
+            pp[c >> 1] = pack_bf16(p0, p1);
+            pp[(c >> 1) + 1] = pack_bf16(p2, p3);
+            dd[c >> 1] = pack_bf16(p0 * (__uint_as_float(dr[c]) - d4.x), p1 * (__uint_as_float(dr[c + 1]) - d4.y));
+            dd[(c >> 1) + 1] =
+                pack_bf16(p2 * (__uint_as_float(dr[c + 2]) - d4.z), p3 * (__uint_as_float(dr[c + 3]) - d4.w));
+          }
+        }
+        if (stamp) dbg_stamp(a, pc, 3);
+        // the previous pair's products must be done before P / dS are overwritten
+        if (prev_i >= 0) {
+          if (!mbar_wait(mma2_done, (pc - 1) & 1, a.err)) { ok = false; break; }
+          tc_fence_after();
+          add_dq(prev_i);
+          if (prev_last_kv) write_dkv(b, h, prev_jt);
+        }
+        if (stamp) dbg_stamp(a, pc, 7);
+        // P^T and dS^T into TMEM (A operands of dV / dK), dS^T into the swizzled smem tile (dQ)
+        tm_st16(lane_base + cP + uint32_t(16 * g), pp);
+        tm_st16(lane_base + cdS + uint32_t(16 * g), dd);
+        {
+          uint8_t* row = sdS + (g >> 1) * 16384 + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int chunk = (4 * (g & 1) + k) ^ (r & 7);
+            *reinterpret_cast<uint4*>(row + chunk * 16) = make_uint4(dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]);
+          }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tm_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_full);
+        if (stamp) dbg_stamp(a, pc, 13);
+        prev_i = it.i;
+        prev_jt = it.jt;
+        prev_last_kv = it.last_of_kv();
+      }
+      if (!ok) break;
+      // ---- item epilogue: the last pair's dQ / dK / dV, then dQ to global ----
+      if (!mbar_wait(mma2_done, (pc - 1) & 1, a.err)) { ok = false; break; }
+      tc_fence_after();
+      add_dq(prev_i);
+      write_dkv(b, h, prev_jt);
+      tc_fence_before();
+      bar_compute();
+      // dQ rows (scaled, bf16) into the Q part of dqkv; pruned rows [0, off) get zeros
+      for (int t = ct; t < a.T; t += kBwdCT) {
+        uint4* dst = reinterpret_cast<uint4*>(a.dqkv + ((int64_t(b) * a.T + t) * 3) * a.H * D + h * D);
+        const int q = t - off;
+        if (q < 0) {
+#pragma unroll
+          for (int c = 0; c < D / 8; ++c) dst[c] = make_uint4(0u, 0u, 0u, 0u);
+        } else {
+#pragma unroll
+          for (int c = 0; c < D / 8; ++c) {
+            const float4 x = reinterpret_cast<const float4*>(sdQ + q * 32)[(2 * c) ^ (q & 7)];
+            const float4 y = reinterpret_cast<const float4*>(sdQ + q * 32)[(2 * c + 1) ^ (q & 7)];
+            uint4 u;
+            u.x = pack_bf16(x.x * a.scale, x.y * a.scale); u.y = pack_bf16(x.z * a.scale, x.w * a.scale);
+            u.z = pack_bf16(y.x * a.scale, y.y * a.scale); u.w = pack_bf16(y.z * a.scale, y.w * a.scale);
+            dst[c] = u;
+          }
+        }
+      }
+      bar_compute();
+      tc_fence_after();
+    }
+    if (!ok) *abort_flag = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+  }
+}
+
 }  // namespace atc
 
 // ---------------------------------------------------------------------------
@@ -508,6 +946,14 @@ void check_qkv5(const at::Tensor& qkv) {
   TORCH_CHECK(reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16 == 0, "qkv must be 16-byte aligned");
 }
 
+// dynamic shared memory of the backward: K, V, Q, dO (two buffers each), the dS
+// tile, lse / delta per query row (padded to whole tiles), the fp32 dQ block, barriers
+size_t bwd_smem_bytes(int q_len) {
+  const int nq = (q_len + atc::kTile - 1) / atc::kTile;
+  const int qrows = (q_len + 7) & ~7;
+  return 1024 + 8 * atc::Geo<32>::kTileBytes + 32768 + 2 * size_t(nq) * atc::kTile * 4 + size_t(qrows) * 128 + 256;
+}
+
 template <int D, int STAGES>
 void launch_fwd(const CUtensorMap& tm, const atc::FwdArgs& a) {
   constexpr size_t used = 1024 + (2 + 2 * STAGES) * atc::Geo<D>::kTileBytes + 256;
@@ -525,6 +971,13 @@ void launch_fwd(const CUtensorMap& tm, const atc::FwdArgs& a) {
 }
 
 }  // namespace
+
+// largest q_len whose fp32 dQ block fits the 227 KB of shared memory
+int64_t fmha_bwd_tc_max_q() {
+  int q = 64;
+  while (bwd_smem_bytes(q + 64) <= 227 * 1024) q += 64;
+  return q;
+}
 
 // qkv [B, T, 3, H, d] (contiguous) -> (o [B, q_len, H, d], lse [B, H, q_len] log2 domain)
 std::vector<at::Tensor> fmha_fwd_tc(at::Tensor qkv, int64_t q_len, double scale, at::Tensor err) {
@@ -546,6 +999,57 @@ std::vector<at::Tensor> fmha_fwd_tc(at::Tensor qkv, int64_t q_len, double scale,
   if (D == 32) launch_fwd<32, 3>(tm, a);
   else launch_fwd<64, 2>(tm, a);
   return {o, lse};
+}
+
+// Backward of fmha_fwd(_tc) for d = 32 into dqkv [B, T, 3, H, d] (fully written).
+void fmha_bwd_tc(at::Tensor qkv, at::Tensor o, at::Tensor lse, at::Tensor dout, at::Tensor dqkv, int64_t q_len,
+                 double scale, at::Tensor err, c10::optional<at::Tensor> dbg) {
+  check_qkv5(qkv);
+  const int B = int(qkv.size(0)), T = int(qkv.size(1)), H = int(qkv.size(3)), D = int(qkv.size(4));
+  TORCH_CHECK(D == 32, "fmha_bwd_tc: head_dim 32 only");
+  TORCH_CHECK(dqkv.sizes() == qkv.sizes() && dqkv.is_contiguous() && dqkv.scalar_type() == at::kBFloat16,
+              "dqkv must be a contiguous bf16 tensor shaped like qkv");
+  TORCH_CHECK(o.is_contiguous() && dout.is_contiguous() && o.dim() == 4 && o.size(0) == B && o.size(1) == q_len &&
+              o.size(2) == H && o.size(3) == D && dout.sizes() == o.sizes() && dout.scalar_type() == at::kBFloat16,
+              "o / dout must be contiguous [B, q_len, H, d]");
+  TORCH_CHECK(lse.is_contiguous() && lse.scalar_type() == at::kFloat && lse.numel() == int64_t(B) * H * q_len);
+  TORCH_CHECK(q_len >= 1 && q_len <= fmha_bwd_tc_max_q(), "fmha_bwd_tc: q_len above the shared-memory cap");
+  if (B == 0) return;
+  atc::BwdArgs a{};
+  a.B = B; a.H = H; a.T = T; a.q_len = int(q_len);
+  a.nq = int((q_len + atc::kTile - 1) / atc::kTile);
+  a.nkv = (T + atc::kTile - 1) / atc::kTile;
+  a.items = B * H;
+  a.c2 = float(scale * 1.4426950408889634);
+  a.scale = float(scale);
+  a.o = reinterpret_cast<const __nv_bfloat16*>(o.data_ptr());
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  a.lse = lse.data_ptr<float>();
+  a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  a.err = err.data_ptr<int>();
+  a.dbg = nullptr;
+  if (dbg && dbg->defined()) {
+    TORCH_CHECK(dbg->is_cuda() && dbg->scalar_type() == at::kLong && dbg->numel() >= atc::kDbgPairs * atc::kDbgSlots,
+                "dbg must be an int64 CUDA tensor of at least 1024 elements");
+    a.dbg = reinterpret_cast<long long*>(dbg->data_ptr());
+  }
+  const CUtensorMap tq = qkv_map(qkv);
+  CUtensorMap td;
+  {
+    cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(H), cuuint64_t(q_len), cuuint64_t(B)};
+    cuuint64_t strides[3] = {cuuint64_t(D * 2), cuuint64_t(H * D * 2), cuuint64_t(q_len * H * D * 2)};
+    cuuint32_t box[4] = {cuuint32_t(D), 1, cuuint32_t(atc::kTile), 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = cuTensorMapEncodeTiled(&td, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, dout.data_ptr(), dims, strides, box,
+                                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled(dout) failed: ", int(r));
+  }
+  const size_t smem = bwd_smem_bytes(int(q_len));
+  PD_CHECK_CUDA(cudaFuncSetAttribute(atc::fmha_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  const int grid = a.items < num_sms() ? a.items : num_sms();
+  atc::fmha_bwd_tc_kernel<<<grid, atc::kBwdThreads, smem, stream()>>>(tq, td, a);
+  PD_CHECK_LAUNCH();
 }
 
 }  // namespace pd

@@ -8,6 +8,9 @@ void fmha_bwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Te
               at::Tensor, double);
 long long launches();
 std::vector<at::Tensor> fmha_fwd_tc(at::Tensor, int64_t, double, at::Tensor);
+void fmha_bwd_tc(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, double, at::Tensor,
+                 c10::optional<at::Tensor>);
+int64_t fmha_bwd_tc_max_q();
 void tc_gemm(at::Tensor, at::Tensor, at::Tensor, int64_t, c10::optional<at::Tensor>, c10::optional<at::Tensor>,
              at::Tensor);
 }  // namespace pd
@@ -16,6 +19,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "primus_dlrm_b200 sm_100a tensor-core kernels";
   m.def("fmha_fwd", &pd::fmha_fwd, "pyramid causal attention forward -> (o, lse)");
   m.def("fmha_fwd_tc", &pd::fmha_fwd_tc, "tcgen05 pyramid causal attention forward from qkv [B,T,3,H,d] -> (o, lse)");
+  m.def("fmha_bwd_tc", &pd::fmha_bwd_tc, py::arg("qkv"), py::arg("o"), py::arg("lse"), py::arg("dout"),
+        py::arg("dqkv"), py::arg("q_len"), py::arg("scale"), py::arg("err"), py::arg("dbg") = py::none(),
+        "tcgen05 attention backward (d=32) into dqkv [B,T,3,H,d]; dbg: optional int64 stage stamps of CTA 0");
+  m.def("fmha_bwd_tc_max_q", &pd::fmha_bwd_tc_max_q, "largest q_len the tcgen05 backward supports");
   m.def("fmha_bwd", &pd::fmha_bwd, "pyramid causal attention backward into dq/dk/dv views");
   m.def("tc_gemm", &pd::tc_gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("epi") = 0,
         py::arg("R") = py::none(), py::arg("AUX") = py::none(), py::arg("err"),

@@ -68,6 +68,13 @@ def _tc_fwd_ok(qkv: torch.Tensor) -> bool:
             and os.environ.get("PD_ATTN_TC_FWD", "0") == "1")
 
 
+def _tc_bwd_ok(qkv: torch.Tensor, q_len: int) -> bool:
+    """tcgen05 backward: contiguous qkv, d = 32, q_len within its shared-memory dQ block."""
+    g = _ext.gemm()
+    return (hasattr(g, "fmha_bwd_tc") and qkv.is_contiguous() and qkv.shape[-1] == 32
+            and q_len <= g.fmha_bwd_tc_max_q() and os.environ.get("PD_ATTN_TC_BWD", "1") != "0")
+
+
 def _err_word(device) -> torch.Tensor:
     w = _ERR.get(device)
     if w is None:
@@ -109,6 +116,9 @@ class _NativeFMHAFused(torch.autograd.Function):
         qkv, o, lse = ctx.saved_tensors
         T, ql = qkv.shape[1], ctx.q_len
         dqkv = torch.empty_like(qkv)
+        if _tc_bwd_ok(qkv, ql):
+            G.fmha_bwd_tc(qkv, o, lse, do.contiguous(), dqkv, ql, ctx.scale, _err_word(qkv.device))
+            return dqkv, None, None
         G.fmha_bwd(qkv[:, T - ql:, 0], qkv[:, :, 1], qkv[:, :, 2], o, lse, do.contiguous(),
                    dqkv[:, :, 0], dqkv[:, :, 1], dqkv[:, :, 2], ctx.scale)
         return dqkv, None, None

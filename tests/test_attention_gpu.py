@@ -101,3 +101,31 @@ def test_fmha_tc_fwd_vs_reference_pyramid_v6_shapes():
         x = qkv.float()
         torch.testing.assert_close(o.float(), _ref(x[:, kl - ql:, 0], x[:, :, 1], x[:, :, 2]), rtol=2e-2, atol=2e-2)
     assert int(err.item()) == 0
+
+
+@pytest.mark.parametrize("ql,kl", [(912, 912), (786, 912), (32, 158), (1, 70), (200, 200), (130, 257), (129, 129),
+                                   (409, 535), (960, 1000)])
+def test_fmha_tc_bwd_matches_reference(ql, kl):
+    """tcgen05 backward (d = 32) vs autograd of the fp32 restatement."""
+    from primus_dlrm_b200.ops import _ext
+    G = _ext.gemm()
+    torch.manual_seed(ql * 5 + kl)
+    B, H, d = 2, 3, 32
+    qkv = torch.randn(B, kl, 3, H, d, device="cuda").to(torch.bfloat16)
+    q, k, v = qkv[:, kl - ql:, 0], qkv[:, :, 1], qkv[:, :, 2]
+    o, lse = G.fmha_fwd(q, k, v, d ** -0.5)
+    do = torch.randn(B, ql, H, d, device="cuda").to(torch.bfloat16)
+    dqkv = torch.full_like(qkv, float("nan"))
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    G.fmha_bwd_tc(qkv, o, lse, do, dqkv, ql, d ** -0.5, err)
+    assert int(err.item()) == 0
+    x = qkv.float().requires_grad_(True)
+    r = _ref(x[:, kl - ql:, 0], x[:, :, 1], x[:, :, 2])
+    r.backward(do.float())
+    g = dqkv.float()
+    assert torch.isfinite(g).all(), "every element of dqkv must be written"
+    for part in range(3):
+        e = (g[:, :, part] - x.grad[:, :, part]).abs().max().item()
+        sc = x.grad[:, :, part].abs().max().item() + 1e-6
+        assert e / sc < 3e-2, f"part {part}: max err {e} (scale {sc})"
+    assert torch.all(g[:, : kl - ql, 0] == 0)
