@@ -70,7 +70,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err
   }
   return true;
 }
-// 5-D tiled TMA load (no multicast) completing on an mbarrier.
+// 5-D tiled TMA load into this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
                                             int c3, int c4) {
   asm volatile(

@@ -5,7 +5,8 @@
 // Structure (one CTA per SM, 6 warps):
 //   warp 0      TMA producer: A/B tiles (128 x 64 and BN x 64, 128-byte
 //               swizzle) into a STAGES-deep shared-memory ring, one mbarrier
-//               per stage with expected-transaction bytes.  No multicast.
+//               per stage with expected-transaction bytes; each CTA loads
+//               its own tiles.
 //   warp 1      allocates TMEM (2 x BN fp32 columns: a double-buffered
 //               accumulator) and one elected lane issues tcgen05.mma
 //               (M=128, N=BN, K=16 per instruction) for every k-step,
