@@ -379,6 +379,16 @@ class _CandidateMixin:
     def _wants(self, name: str) -> bool:
         return any(d.name == name for d in self.config.feature.dense_features)
 
+    def _dense_dim(self, name: str, default: int) -> int:
+        for d in self.config.feature.dense_features:
+            if d.name == name:
+                return d.dim
+        return default
+
+    def _counters_on(self) -> bool:
+        st = getattr(self, "store", None)
+        return bool(self.config.data.enable_counters and st is not None and st.enable_counters)
+
     def user_batch(self, sample: dict, device) -> dict[str, torch.Tensor]:
         h = sample["history"]
         out = {f"hist_{p}_{k}_ids": torch.from_numpy(np.asarray(h[f"{p}_{k}s"])).long().unsqueeze(0).to(device)
@@ -465,15 +475,21 @@ class YambdaEvalDataset(_YambdaBase, _CandidateMixin):
 
     def get_user_counters(self, uid: int) -> np.ndarray:
         s, e = self.store.user_slice(uid)
-        if s < 0 or not self.store.enable_counters:
-            return np.zeros(3 * len(self.config.data.counter_windows_days), np.float32)
+        if s < 0 or not self._counters_on():
+            return np.zeros(self._dense_dim("user_counters", 3 * len(self.config.data.counter_windows_days)),
+                            np.float32)
         return np.asarray(self.store.user_counters[e - 1]).copy()
 
     def get_item_counters_batch(self, items: np.ndarray) -> np.ndarray:
+        if not self._counters_on():
+            W = len(self.config.data.counter_windows_days)
+            return np.zeros((len(items), self._dense_dim("item_counters", 3 * W)), np.float32)
         return self.eval_item_counters[items]
 
     def get_cross_counters_batch(self, uid: int, items: np.ndarray) -> np.ndarray:
         W = len(self.config.data.counter_windows_days)
+        if not self._counters_on():
+            return np.zeros((len(items), self._dense_dim("cross_counters", 9 * W)), np.float32)
         out = np.zeros((len(items), 9 * W), np.float32)
         s, e = self.store.user_slice(uid)
         if s < 0:
