@@ -207,6 +207,10 @@ def main() -> None:
         dist.barrier()
     e2e_ms = (time.perf_counter() - t0) * 1000 / args.steps
     clocks = sampler.stop() if sampler else None
+    # device error words of the peer-memory collectives (bounded waits that ran out)
+    for obj in (ex, engine.grad_sync):
+        if obj is not None and hasattr(obj, "check"):
+            obj.check()
 
     stats = torch.tensor([ms, e2e_ms, float(launches), a2a_ms], device=device, dtype=torch.float64)
     if world > 1:

@@ -40,6 +40,8 @@ void ipc_close(int64_t);
 void push_rows(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor);
 void signal_barrier(at::Tensor, int64_t, int64_t, int64_t, at::Tensor);
 at::Tensor owner_keys(at::Tensor, at::Tensor, int64_t);
+void peer_reduce_slice(at::Tensor, int64_t, at::Tensor, int64_t, int64_t, double);
+void peer_gather_slices(at::Tensor, int64_t, at::Tensor, at::Tensor);
 }  // namespace pd
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -68,5 +70,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("push_rows", &pd::push_rows);
   m.def("signal_barrier", &pd::signal_barrier);
   m.def("owner_keys", &pd::owner_keys);
+  m.def("peer_reduce_slice", &pd::peer_reduce_slice, "own[a:b) = scale * sum over ranks of peer[a:b) (NVLink P2P loads)");
+  m.def("peer_gather_slices", &pd::peer_gather_slices, "copy every other rank's slice from that rank (all-gather)");
   m.def("launch_count", &pd::launches, "kernels launched by this extension so far");
 }

@@ -189,6 +189,102 @@ void signal_barrier(at::Tensor pads, int64_t rank, int64_t epoch, int64_t timeou
 }
 
 // ---------------------------------------------------------------------------
+// dense gradient / parameter collectives over peer memory
+//
+// Every rank's flat fp32 buffer is mapped into every rank (CUDA IPC), and
+// the buffer is split into W slices (64-element aligned). Between signal
+// barriers:
+//   peer_reduce_slice: this rank's slice = scale * sum over ranks of that
+//     slice, read with L1-bypassing loads from each peer (NVLink P2P), written
+//     into this rank's own buffer (two-shot reduce-scatter, first half);
+//   peer_gather_slices: every other rank's (final) slice is copied from that
+//     rank into this rank's buffer (second half, an all-gather).
+// Slices are disjoint, so no rank writes memory another rank reads in the
+// same phase; the barrier after the gather keeps a rank from reusing its
+// buffer while peers still read it.
+// ---------------------------------------------------------------------------
+constexpr int kMaxPeers = 16;
+struct PeerBufs {
+  const float* buf[kMaxPeers];
+  int world;
+  int rank;
+};
+
+__global__ void __launch_bounds__(512) peer_reduce_slice_kernel(const __grid_constant__ PeerBufs P, float* __restrict__ own,
+                                                                int64_t a, int64_t b, float scale) {
+  const int64_t n4 = (b - a) >> 2;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const int64_t off = a + 4 * i;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int p = 0; p < P.world; ++p) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(P.buf[p] + off));
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    acc.x *= scale; acc.y *= scale; acc.z *= scale; acc.w *= scale;
+    *reinterpret_cast<float4*>(own + off) = acc;
+  }
+}
+
+__global__ void __launch_bounds__(512) peer_gather_slices_kernel(const __grid_constant__ PeerBufs P, float* __restrict__ own,
+                                                                 const int64_t* __restrict__ bounds) {
+  // bounds: [world + 1] slice boundaries (elements); blockIdx.y = source rank
+  const int src = blockIdx.y;
+  if (src == P.rank) return;
+  const int64_t a = bounds[src], b = bounds[src + 1];
+  const int64_t n4 = (b - a) >> 2;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  const float* from = P.buf[src];
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const int64_t off = a + 4 * i;
+    *reinterpret_cast<float4*>(own + off) = __ldcg(reinterpret_cast<const float4*>(from + off));
+  }
+}
+
+static PeerBufs peer_bufs(const at::Tensor& ptrs, int64_t rank) {
+  const int W = int(ptrs.numel());
+  TORCH_CHECK(W >= 1 && W <= kMaxPeers && rank >= 0 && rank < W, "1..16 ranks");
+  PeerBufs P;
+  P.world = W;
+  P.rank = int(rank);
+  auto a = ptrs.accessor<int64_t, 1>();
+  for (int r = 0; r < W; ++r) {
+    P.buf[r] = reinterpret_cast<const float*>(static_cast<uintptr_t>(a[r]));
+    TORCH_CHECK(a[r] % 16 == 0, "peer buffers must be 16-byte aligned");
+  }
+  return P;
+}
+
+// own[a:b) = scale * sum_r peer_r[a:b); a, b multiples of 4.
+void peer_reduce_slice(at::Tensor ptrs, int64_t rank, at::Tensor own, int64_t a, int64_t b, double scale) {
+  TORCH_CHECK(own.is_cuda() && own.scalar_type() == at::kFloat && own.is_contiguous());
+  TORCH_CHECK(a >= 0 && b <= own.numel() && a % 4 == 0 && b % 4 == 0 && a <= b, "slice must be 4-aligned");
+  const PeerBufs P = peer_bufs(ptrs, rank);
+  if (b == a) return;
+  int64_t blocks = ((b - a) / 4 + 511) / 512;
+  const int64_t cap = int64_t(num_sms()) * 4;
+  if (blocks > cap) blocks = cap;
+  peer_reduce_slice_kernel<<<blocks, 512, 0, stream()>>>(P, own.data_ptr<float>(), a, b, float(scale));
+  PD_CHECK_LAUNCH();
+}
+
+// own[slice q] = peer_q[slice q] for every q != rank; bounds: int64 CUDA [W + 1].
+void peer_gather_slices(at::Tensor ptrs, int64_t rank, at::Tensor own, at::Tensor bounds) {
+  TORCH_CHECK(own.is_cuda() && own.scalar_type() == at::kFloat && own.is_contiguous());
+  TORCH_CHECK(bounds.is_cuda() && bounds.scalar_type() == at::kLong && bounds.numel() == ptrs.numel() + 1);
+  const PeerBufs P = peer_bufs(ptrs, rank);
+  const int64_t per = own.numel() / P.world + 1;
+  int64_t blocks = (per / 4 + 511) / 512;
+  const int64_t cap = int64_t(num_sms()) * 4 / (P.world > 1 ? P.world - 1 : 1) + 1;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  peer_gather_slices_kernel<<<dim3(unsigned(blocks), unsigned(P.world)), 512, 0, stream()>>>(
+      P, own.data_ptr<float>(), bounds.data_ptr<int64_t>());
+  PD_CHECK_LAUNCH();
+}
+
+// ---------------------------------------------------------------------------
 // owner of each (table, row) key; composite sort key = owner << 44 | key
 // ---------------------------------------------------------------------------
 constexpr int kMaxTablesComm = 32;

@@ -17,7 +17,10 @@
 //               back to the MMA warp.  The MMA of tile i+1 overlaps the
 //               epilogue of tile i.
 // Fused epilogues: none | GELU (optionally also storing the pre-activation) |
-// residual add | GELU backward (acc * gelu'(pre)).
+// residual add | GELU backward (acc * gelu'(pre)). An addend R (residual, or
+// a bias / positional table broadcast through zero strides) is added before
+// the activation in every mode but the GELU backward, where R is the
+// pre-activation.
 //
 // A and B are described by 3-D TMA maps {K, rows, L} with arbitrary row and
 // batch strides, so strided views (e.g. the NS rows of every sample, one
@@ -278,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     uint8_t* stX = stR;   // GELU (AUX) and residual/dGELU (R) never occur together
     const int cr = lane >> 2, cc = lane & 3;
     auto sw = [](int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); };
-    const bool has_r = (p.epi == kResidual || p.epi == kDGelu);
+    const bool has_r = (p.R != nullptr);   // addend (bias / residual), or GELU's pre-activation for kDGelu
     // work items: (tile, chunk) in this warp's order
     auto first_chunk = [&]() { return part * 32; };
     auto next_work = [&](int& t, int& c) {
@@ -321,6 +324,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
         float v[32];
         tc_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(a * BN + c), v);
+        if (has_r && p.epi != kDGelu) {
+          // addend before the activation: residual, or a bias broadcast through a zero row stride
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 pk = *reinterpret_cast<const uint4*>(stR + sw(lane, j));
+            const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&pk);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __bfloat1622float2(hh[e]);
+              v[8 * j + 2 * e] += f.x;
+              v[8 * j + 2 * e + 1] += f.y;
+            }
+          }
+        }
         if (p.epi == kGelu && p.AUX) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -337,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (p.epi == kGelu) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu_f(__bfloat162float(__float2bfloat16_rn(v[j])));
-        } else if (has_r) {
+        } else if (p.epi == kDGelu) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint4 pk = *reinterpret_cast<const uint4*>(stR + sw(lane, j));
@@ -345,8 +362,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 f = __bfloat1622float2(h[e]);
-              if (p.epi == kResidual) { v[8 * j + 2 * e] += f.x; v[8 * j + 2 * e + 1] += f.y; }
-              else { v[8 * j + 2 * e] *= gelu_grad_f(f.x); v[8 * j + 2 * e + 1] *= gelu_grad_f(f.y); }
+              v[8 * j + 2 * e] *= gelu_grad_f(f.x);
+              v[8 * j + 2 * e + 1] *= gelu_grad_f(f.y);
             }
           }
         }
@@ -468,8 +485,10 @@ void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optiona
   p.C = reinterpret_cast<__nv_bfloat16*>(C.data_ptr()); p.c_ls = C.stride(0); p.c_ms = C.stride(1);
   p.epi = int(epi);
   p.err = err.data_ptr<int>();
-  if (epi == tc::kResidual || epi == tc::kDGelu) {
-    TORCH_CHECK(R && R->dim() == 3 && R->sizes() == C.sizes() && R->stride(2) == 1 && R->stride(1) % 8 == 0 &&
+  TORCH_CHECK(!(epi == tc::kResidual || epi == tc::kDGelu) || (R && R->defined()), "this epilogue needs R");
+  if (R && R->defined()) {
+    // R: [L, M, N] view (stride 0 allowed on L and M: a bias or per-row-block addend)
+    TORCH_CHECK(R->dim() == 3 && R->sizes() == C.sizes() && R->stride(2) == 1 && R->stride(1) % 8 == 0 &&
                 (R->size(0) == 1 || R->stride(0) % 8 == 0) && reinterpret_cast<uintptr_t>(R->data_ptr()) % 16 == 0 &&
                 R->scalar_type() == at::kBFloat16, "R must match C (bf16, 16-byte aligned rows)");
     p.R = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr()); p.r_ls = R->stride(0); p.r_ms = R->stride(1);

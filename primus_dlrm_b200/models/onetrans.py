@@ -156,10 +156,8 @@ class SequentialTokenizer(nn.Module):
         self.pos_emb = nn.Embedding(max_len, d_model) if use_pos_embed else None
 
     def forward(self, raw: torch.Tensor) -> torch.Tensor:
-        tok = dense.mlp2(raw, self.proj[0], self.proj[2])
-        if self.pos_emb is not None:
-            tok = tok + self.pos_emb.weight[: tok.shape[1]].to(tok.dtype)
-        return tok
+        pos = self.pos_emb.weight[: raw.shape[1]] if self.pos_emb is not None else None
+        return dense.mlp2(raw, self.proj[0], self.proj[2], addend=pos)
 
 
 class AutoSplitTokenizer(nn.Module):
@@ -304,6 +302,92 @@ class OneTransModel(BaseModel):
         """(total, {task: loss}, {task: logits}) with heads + loss fused."""
         h, _, _ = self._backbone(batch)
         return fused_heads_loss(self.heads, h, batch, loss_weights, regression_tasks)
+
+    # ------------------------------------------------------------------
+    @torch.no_grad()
+    def score_candidates(self, user_batch: dict[str, torch.Tensor], candidate_batch: dict[str, torch.Tensor],
+                         task: str, batch_size: int = 1024) -> torch.Tensor:
+        """Scores [C] of one user against C candidates with an S-side K/V cache.
+
+        S tokens sit before the NS tokens and attention is causal, so the S
+        stream (hidden states, and the keys / values of every layer) depends
+        on the user's history only: it is computed once, for a batch of one,
+        following the pyramid. Each candidate then runs only its NS tokens,
+        attending to the cached S keys / values plus its own NS keys -- the
+        same function as ``forward`` on (user history, candidate), at the cost
+        of n_ns tokens per candidate instead of L_S + n_ns
+        (``primus_dlrm/evaluation/metrics.py:200-279`` recomputes everything).
+        """
+        ot = self.config.model.transformer
+        n_ns, H = ot.n_ns_tokens, ot.n_heads
+        D = ot.d_model
+        dh = D // H
+        C = next(iter(candidate_batch.values())).shape[0]
+        # ---- user side: S tokens through the pyramid, caching per-layer K / V ----
+        f2k = self.config.feature_to_batch_key()
+        fc = self.config.feature
+        seq = {f: user_batch[f2k.get(f, f)] for feats in fc.sequence_groups.values() for f in feats}
+        pools = self.emb.lookup_groups(seq, [list(v) for v in fc.sequence_groups.values()],
+                                       dtype=self._compute_dtype(user_batch))
+        xs = torch.cat([tok(raw) for tok, raw in zip(self.seq_tokenizers.values(), pools)], dim=1)  # [1, L_S, D]
+        L_S = xs.shape[1]
+        sched = pyramid_schedule(L_S, n_ns, ot.n_layers) if ot.use_pyramid else [L_S] * ot.n_layers
+        cache = []
+        for l, blk in enumerate(self.blocks):
+            at = blk.attn
+            h = blk.norm1(xs)
+            qkv = (h @ at.s_qkv.weight.t().to(h.dtype)).view(1, -1, 3, H, dh)
+            q_s = sched[l]                                   # S queries kept by this layer
+            k_s, v_s = qkv[:, :, 1], qkv[:, :, 2]            # [1, n_s, H, dh]
+            cache.append((k_s, v_s))
+            n_s = xs.shape[1]
+            q = qkv[:, n_s - q_s:, 0]
+            o = pyramid_attention(q, k_s, v_s, impl="mask").reshape(1, q_s, D)
+            z = at.out_proj(o) + xs[:, n_s - q_s:]
+            y = blk.norm2(z)
+            xs = z + blk.ffn.s_w2(F.gelu(blk.ffn.s_w1(y)))
+        # ---- candidate side: NS tokens only ----
+        scores = []
+        for c0 in range(0, C, batch_size):
+            c1 = min(C, c0 + batch_size)
+            cb = {k: v[c0:c1] for k, v in candidate_batch.items()}
+            nb = c1 - c0
+            for k, v in user_batch.items():
+                if k not in cb:
+                    cb[k] = v.expand(nb, *v.shape[1:])
+            ns_raw = self._ns_raw(cb)
+            x = self.ns_tokenizer(ns_raw)                    # [nb, n_ns, D]
+            for l, blk in enumerate(self.blocks):
+                at = blk.attn
+                k_s, v_s = cache[l]
+                n_s = k_s.shape[1]
+                h = blk.norm1(x)
+                qkv = torch.einsum("btk,tnk->btn", h, at.ns_qkv_weight.to(h.dtype)).view(nb, n_ns, 3, H, dh)
+                q, k_n, v_n = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+                k = torch.cat([k_s.expand(nb, -1, -1, -1).to(k_n.dtype), k_n], dim=1)
+                v = torch.cat([v_s.expand(nb, -1, -1, -1).to(v_n.dtype), v_n], dim=1)
+                o = pyramid_attention(q, k, v, impl="mask").reshape(nb, n_ns, D)
+                z = at.out_proj(o) + x
+                y = blk.norm2(z)
+                f = torch.einsum("btk,tnk->btn", y, blk.ffn.ns_w1.to(y.dtype))
+                f = torch.einsum("btk,tnk->btn", F.gelu(f), blk.ffn.ns_w2.to(y.dtype))
+                x = z + f
+            x = self.final_norm(x)
+            hh = self.head_proj(x.reshape(nb, -1))
+            scores.append(self.heads[task](hh).squeeze(-1).float())
+        return torch.cat(scores)
+
+    def _ns_raw(self, batch: dict[str, torch.Tensor]) -> torch.Tensor:
+        """The NS tokenizer input of a batch: scalar embeddings + dense features."""
+        f2k = self.config.feature_to_batch_key()
+        fc = self.config.feature
+        feats = {f: batch[f2k.get(f, f)] for f in fc.scalar_feature_names if f2k.get(f, f) in batch}
+        scal = self.emb.lookup_groups(feats, [list(fc.scalar_feature_names)], dtype=self._compute_dtype(batch))[0]
+        parts = [scal]
+        for df in fc.dense_features:
+            xd = batch[df.name]
+            parts.append(self.dense_projs[df.name](xd) if df.name in self.dense_projs else xd.to(scal.dtype))
+        return torch.cat([p.to(scal.dtype) for p in parts], dim=-1)
 
     def forward_with_cross_scores(self, batch: dict[str, torch.Tensor], cross_task: str = ""):
         h, s_repr, scal = self._backbone(batch)

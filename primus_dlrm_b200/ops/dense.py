@@ -225,6 +225,69 @@ def mixed_linear(x: torch.Tensor, n_s: int, w_s: torch.Tensor, w_ns: torch.Tenso
     return y
 
 
-def mlp2(x: torch.Tensor, l1: nn.Linear, l2: nn.Linear) -> torch.Tensor:
-    """l2(GELU(l1(x)))."""
-    return l2(F.gelu(l1(x)))
+class _MLP2Native(torch.autograd.Function):
+    """y = W2 GELU(W1 x + b1) + b2 (+ addend[l]) on the tcgen05 GEMM: the bias
+    and GELU (with the pre-activation stored for backward) fused into the
+    first GEMM's epilogue, bias + per-position addend (the tokenizer's
+    positional embedding) into the second's, GELU' into the data-gradient
+    GEMM. x [B, L, K]; addend [L, N] or None."""
+
+    @staticmethod
+    def forward(ctx, x, w1, b1, w2, b2, addend):
+        xb = x.contiguous().to(torch.bfloat16)
+        B, L, K = xb.shape
+        F_, N = w1.shape[0], w2.shape[0]
+        w1b, w2b = w1.to(torch.bfloat16), w2.to(torch.bfloat16)
+        rows = B * L
+        v = lambda t: t.reshape(1, rows, t.shape[-1])  # noqa: E731
+        r1 = b1.to(torch.bfloat16).reshape(1, 1, F_).expand(1, rows, F_)
+        h = torch.empty(B, L, F_, dtype=torch.bfloat16, device=x.device)
+        pre = torch.empty_like(h)
+        tc_gemm(v(xb), w1b.reshape(1, F_, K), v(h), "gelu", R=r1, AUX=v(pre))
+        add2 = b2.to(torch.bfloat16).reshape(1, N)
+        if addend is not None:
+            add2 = (addend.to(torch.float32) + b2.to(torch.float32)).to(torch.bfloat16)
+            r2 = add2.reshape(1, L, N).expand(B, L, N)
+        else:
+            r2 = add2.reshape(1, 1, N).expand(B, L, N)
+        out = torch.empty(B, L, N, dtype=torch.bfloat16, device=x.device)
+        tc_gemm(v(h), w2b.reshape(1, N, F_), v(out), None, R=v(r2))
+        ctx.save_for_backward(xb, h, pre, w1b, w2b)
+        ctx.meta = (w1.dtype, b1.dtype, w2.dtype, b2.dtype, addend is not None,
+                    addend.dtype if addend is not None else None)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        xb, h, pre, w1b, w2b = ctx.saved_tensors
+        dt_w1, dt_b1, dt_w2, dt_b2, has_add, dt_add = ctx.meta
+        dout = dout.contiguous().to(torch.bfloat16)
+        B, L, N = dout.shape
+        F_, K = w1b.shape
+        rows = B * L
+        v = lambda t: t.reshape(1, rows, t.shape[-1])  # noqa: E731
+        dpre = torch.empty(B, L, F_, dtype=torch.bfloat16, device=dout.device)
+        tc_gemm(v(dout), w2b.t().contiguous().reshape(1, F_, N), v(dpre), "dgelu", R=v(pre))
+        dx = torch.empty(B, L, K, dtype=torch.bfloat16, device=dout.device)
+        tc_gemm(v(dpre), w1b.t().contiguous().reshape(1, K, F_), v(dx))
+        d2 = dout.reshape(rows, N)
+        dp = dpre.reshape(rows, F_)
+        dw2 = torch.matmul(d2.t(), h.reshape(rows, F_)).to(dt_w2)
+        dw1 = torch.matmul(dp.t(), xb.reshape(rows, K)).to(dt_w1)
+        dpos = dout.float().sum(0)                      # [L, N]
+        db2 = dpos.sum(0).to(dt_b2)
+        db1 = dp.float().sum(0).to(dt_b1)
+        return dx, dw1, db1, dw2, db2, (dpos.to(dt_add) if has_add else None)
+
+
+def mlp2(x: torch.Tensor, l1: nn.Linear, l2: nn.Linear, addend: torch.Tensor | None = None) -> torch.Tensor:
+    """l2(GELU(l1(x))) (+ addend[:L] broadcast over the batch).  On the
+    tcgen05 GEMM when the shapes allow (bf16, K % 8, hidden / output % 64)."""
+    if (x.dim() == 3 and _gemm_ok(x) and x.dtype == torch.bfloat16 and l1.bias is not None
+            and l2.bias is not None and _tc_ok(x, l1.in_features, l1.out_features)
+            and l2.out_features % 64 == 0 and l1.out_features % 8 == 0):
+        return _MLP2Native.apply(x, l1.weight, l1.bias, l2.weight, l2.bias, addend)
+    y = l2(F.gelu(l1(x)))
+    if addend is not None:
+        y = y + addend.to(y.dtype)
+    return y

@@ -50,6 +50,11 @@ class FlatParams:
             if g is None or g.data_ptr() != self.grad[off:].data_ptr():
                 p.grad = self.grad[off:off + p.numel()].view_as(p)
 
+    def rebind_all(self) -> None:
+        """Re-point every param's data at ``self.data`` (after the arena moved)."""
+        for p, off in zip(self.params, self.offsets):
+            p.data = self.data[off:off + p.numel()].view_as(p)
+
     def rebind(self) -> None:
         """Re-point params at the arena (after e.g. ``load_state_dict`` replaced data)."""
         for p, off in zip(self.params, self.offsets):

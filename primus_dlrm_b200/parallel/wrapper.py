@@ -7,10 +7,13 @@
   otherwise they are replicated (data-parallel with a sparse gradient
   all-gather), which is what the reference's plain DDP run does;
 * dense parameters are broadcast from rank 0 and their gradients are
-  synchronised by ``FlatGradSync`` (``ddp`` / ``dmp``: all-reduce of the flat
-  gradient arena in buckets) or ``ShardedGradSync`` (``fsdp``:
-  reduce-scatter of gradients, AdamW on this rank's 1/W slice, all-gather of
-  parameters -- optimizer state and gradients sharded ZeRO-style).
+  synchronised over NVLink peer memory on CUDA (``distributed.comm: peer``):
+  ``PeerGradSync`` (``ddp`` / ``dmp``: two-shot all-reduce of the flat
+  gradient arena by slice kernels) or ``PeerShardedGradSync`` (``fsdp``:
+  slice reduce-scatter, AdamW on this rank's 1/W slice, parameter
+  all-gather -- optimizer state and gradients sharded ZeRO-style). With
+  ``comm: nccl`` (and on CPU / gloo) the same strategies run as NCCL
+  collectives (``FlatGradSync`` / ``ShardedGradSync``), the baseline.
 
 ``distributed.comm`` picks the sparse exchange: ``peer`` (NVLink peer-memory
 kernels, CUDA) or ``nccl`` (collective baseline; also the CPU/gloo path).
@@ -87,6 +90,119 @@ class ShardedGradSync:
         flat_data.copy_(full[:n])
 
 
+class _PeerDense:
+    """Shared machinery of the peer-memory dense collectives: a flat fp32
+    buffer mapped into every rank, a signal pad for bounded barriers, and the
+    64-element aligned slice boundaries (rank r owns [bounds[r], bounds[r+1]))."""
+
+    def __init__(self, numel: int, device: torch.device, group=None, timeout_s: float = 60.0):
+        from primus_dlrm_b200.ops import _ext
+        from primus_dlrm_b200.parallel.sharded_embedding import SymmetricBuffer
+        self.C = _ext.core()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.numel = int(numel)
+        per = (-(-self.numel // self.world) + 63) // 64 * 64
+        self.per = per
+        b = [min(r * per, self.numel) for r in range(self.world + 1)]
+        self.bounds = torch.tensor(b, dtype=torch.int64, device=device)
+        self.slice = (b[self.rank], b[self.rank + 1])
+        self.mem = SymmetricBuffer(per * self.world * 4, device, self.rank, self.world, group)
+        self.buf = self.mem.local[: self.numel * 4].view(torch.float32)
+        self.ptrs = torch.tensor(self.mem.ptrs, dtype=torch.int64)
+        self.pads = SymmetricBuffer(64 * 8, device, self.rank, self.world, group)
+        self.pad_ptrs = torch.tensor(self.pads.ptrs, dtype=torch.int64)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.epoch = 0
+
+    def barrier(self) -> None:
+        self.epoch += 1
+        self.C.signal_barrier(self.pad_ptrs, self.rank, self.epoch, self.timeout_ns, self.err)
+
+    def check(self) -> None:
+        code = int(self.err.item())
+        if code:
+            raise RuntimeError(f"peer dense collective on rank {self.rank}: error word {code} "
+                               f"(2 = a peer did not reach a barrier in time)")
+
+    def reduce_scatter(self, scale: float) -> None:
+        a, b = self.slice
+        self.barrier()
+        self.C.peer_reduce_slice(self.ptrs, self.rank, self.buf, a, b, scale)
+
+    def all_gather(self) -> None:
+        self.barrier()
+        self.C.peer_gather_slices(self.ptrs, self.rank, self.buf, self.bounds)
+        self.barrier()
+
+
+class PeerGradSync(_PeerDense):
+    """DDP gradient averaging over NVLink peer memory (two-shot all-reduce:
+    each rank reduces its 1/W slice from every peer's arena, then gathers the
+    other slices). The flat gradient arena itself lives in the shared buffer
+    (``bind``), so backward writes straight into memory the peers read."""
+
+    def __init__(self, numel: int, device: torch.device, group=None, timeout_s: float = 60.0):
+        super().__init__(numel, device, group, timeout_s)
+
+    def bind(self, flat) -> None:
+        self.buf.copy_(flat.grad)
+        flat.grad = self.buf
+        flat.zero_grad()
+
+    def sync(self, flat_grad: torch.Tensor) -> None:
+        if flat_grad.data_ptr() != self.buf.data_ptr():
+            self.buf.copy_(flat_grad)
+        self.reduce_scatter(1.0 / self.world)
+        self.all_gather()
+        if flat_grad.data_ptr() != self.buf.data_ptr():
+            flat_grad.copy_(self.buf)
+
+
+class PeerShardedGradSync(_PeerDense):
+    """ZeRO-style sharding over peer memory (``fsdp``): gradients are
+    reduce-scattered by the slice kernel (each rank keeps the average of its
+    slice), AdamW updates that slice, and parameters are all-gathered from
+    the owners' arenas. Parameters and gradients both live in shared buffers."""
+
+    sharded = True
+
+    def __init__(self, numel: int, device: torch.device, group=None, timeout_s: float = 60.0):
+        super().__init__(numel, device, group, timeout_s)
+        self.params = _PeerDense(numel, device, group, timeout_s)
+
+    def shard_range(self, n: int) -> tuple[int, int]:
+        return self.slice
+
+    def bind(self, flat) -> None:
+        self.buf.copy_(flat.grad)
+        flat.grad = self.buf
+        self.params.buf.copy_(flat.data)
+        flat.data = self.params.buf
+        flat.rebind_all()
+        flat.zero_grad()
+
+    def sync(self, flat_grad: torch.Tensor) -> None:
+        if flat_grad.data_ptr() != self.buf.data_ptr():
+            self.buf.copy_(flat_grad)
+        self.reduce_scatter(1.0 / self.world)
+        # peers read this arena during the reduction; wait before it is reused
+        self.barrier()
+
+    def gather_params(self, flat_data: torch.Tensor) -> None:
+        if flat_data.data_ptr() != self.params.buf.data_ptr():
+            self.params.buf.copy_(flat_data)
+        self.params.all_gather()
+        if flat_data.data_ptr() != self.params.buf.data_ptr():
+            flat_data.copy_(self.params.buf)
+
+    def check(self) -> None:
+        super().check()
+        self.params.check()
+
+
 def broadcast_dense(model: nn.Module, group=None) -> None:
     for p in model.parameters():
         if p.requires_grad:
@@ -115,15 +231,43 @@ def wrap_model(model: nn.Module, device: torch.device, config, group=None):
                          seed=config.train.seed, init=config.model.embedding_init)
     model = model.to(device)
     broadcast_dense(model, group)
-    if dc.dense_strategy == "fsdp":
-        sync = ShardedGradSync(group)
-    elif dc.dense_strategy in ("ddp", "dmp"):
-        sync = FlatGradSync(group)
-    else:
+    peer = device.type == "cuda" and dc.comm == "peer"
+    if dc.dense_strategy not in ("fsdp", "ddp", "dmp"):
         raise ValueError(f"Unknown dense_strategy: {dc.dense_strategy!r}")
+    if peer:
+        # sized by the flat arena the engine builds (bind() is called with it)
+        sync = _LazyPeerSync(device, group, sharded=dc.dense_strategy == "fsdp")
+    elif dc.dense_strategy == "fsdp":
+        sync = ShardedGradSync(group)
+    else:
+        sync = FlatGradSync(group)
     logger.info("wrapped for %d ranks: dense=%s embeddings=%s comm=%s", world, dc.dense_strategy,
                 "sharded" if emb is not None and emb.sharded else "none", dc.comm)
     return model, sync
+
+
+class _LazyPeerSync:
+    """Placeholder until the engine's flat arena exists: ``bind(flat)``
+    builds the peer collective of the right size and becomes it."""
+
+    def __init__(self, device, group, sharded: bool):
+        self.device, self.group, self._sharded = device, group, sharded
+        self.impl = None
+
+    @property
+    def sharded(self) -> bool:
+        return self._sharded
+
+    def bind(self, flat) -> None:
+        cls = PeerShardedGradSync if self._sharded else PeerGradSync
+        self.impl = cls(flat.numel, self.device, self.group)
+        self.impl.bind(flat)
+
+    def __getattr__(self, name):
+        impl = self.__dict__.get("impl")
+        if impl is None:
+            raise AttributeError(f"peer gradient sync used before bind(): {name}")
+        return getattr(impl, name)
 
 
 def _has_meta_dense(model: nn.Module) -> bool:

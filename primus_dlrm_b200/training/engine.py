@@ -58,6 +58,8 @@ class TrainEngine:
         self.loss_fn = MultiTaskLoss(tc.loss_weights, tc.regression_tasks)
         self.bpr = InBatchBPRLoss(tc.contrastive_temperature) if tc.contrastive_weight > 0 else None
         self.grad_sync = grad_sync
+        if grad_sync is not None and hasattr(grad_sync, "bind"):
+            grad_sync.bind(self.flat)      # peer collectives: the arenas live in shared memory
         self.global_step = 0
         self.skipped_steps = 0
         self.use_amp = tc.bf16

@@ -106,3 +106,45 @@ def test_gelu_epilogue_accuracy_vs_exact_erf():
     xg = x.clone().requires_grad_(True)
     F.gelu(xg).backward(torch.ones_like(xg))
     torch.testing.assert_close(c[0, 0].float(), xg.grad.to(torch.bfloat16).float(), rtol=0, atol=1e-2)
+
+
+def test_gemm_bias_addend_before_gelu():
+    """R broadcast through zero strides is added before the activation."""
+    from primus_dlrm_b200.ops.dense import tc_gemm
+    torch.manual_seed(3)
+    M, N, K = 1000, 256, 384
+    A = torch.randn(1, M, K, device="cuda").to(torch.bfloat16)
+    W = (torch.randn(1, N, K, device="cuda") / K ** 0.5).to(torch.bfloat16)
+    b = torch.randn(N, device="cuda").to(torch.bfloat16)
+    C = torch.empty(1, M, N, dtype=torch.bfloat16, device="cuda")
+    pre = torch.empty_like(C)
+    tc_gemm(A, W, C, "gelu", R=b.reshape(1, 1, N).expand(1, M, N), AUX=pre)
+    ref_pre = A.float()[0] @ W.float()[0].t() + b.float()
+    torch.testing.assert_close(pre.float()[0], ref_pre, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(C.float()[0], torch.nn.functional.gelu(ref_pre), rtol=2e-2, atol=2e-2)
+
+
+def test_tokenizer_mlp_native_matches_torch():
+    """Fused tokenizer MLP (bias + GELU, bias + positional addend) fwd / bwd vs fp32."""
+    from primus_dlrm_b200.ops.dense import mlp2
+    torch.manual_seed(4)
+    B, L, K, D = 16, 40, 384, 256
+    l1 = torch.nn.Linear(K, D).cuda()
+    l2 = torch.nn.Linear(D, D).cuda()
+    pos = torch.nn.Parameter(torch.randn(64, D, device="cuda") * 0.1)
+    x = torch.randn(B, L, K, device="cuda").to(torch.bfloat16).requires_grad_(True)
+    y = mlp2(x, l1, l2, addend=pos[:L])
+    assert y.dtype == torch.bfloat16
+    g = torch.randn_like(y)
+    y.backward(g)
+    grads = [t.grad.clone() for t in (l1.weight, l1.bias, l2.weight, l2.bias, pos)] + [x.grad.float().clone()]
+    for t in (l1.weight, l1.bias, l2.weight, l2.bias, pos):
+        t.grad = None
+    xr = x.detach().float().requires_grad_(True)
+    yr = l2(torch.nn.functional.gelu(l1(xr))) + pos[:L]
+    torch.testing.assert_close(y.float(), yr, rtol=3e-2, atol=3e-2)
+    yr.backward(g.float())
+    ref = [t.grad for t in (l1.weight, l1.bias, l2.weight, l2.bias, pos)] + [xr.grad]
+    for got, exp in zip(grads, ref):
+        err = (got.float() - exp).abs().max().item()
+        assert err / (exp.abs().max().item() + 1e-6) < 3e-2

@@ -243,3 +243,44 @@ def test_bpr_loss_value():
     y = torch.tensor([1.0, 0.0])
     exp = -torch.nn.functional.logsigmoid(torch.tensor((2.0 - 0.0) / 0.1))
     torch.testing.assert_close(InBatchBPRLoss(0.1)(s, y), exp)
+
+
+@pytest.mark.parametrize("pyramid", [True, False])
+def test_onetrans_kv_cached_scoring_is_exact(pyramid):
+    """score_candidates (S stream once, NS tokens per candidate) == forward on
+    (user history, candidate) rows."""
+    cfg = _config("onetrans", windows=2, transformer={"use_pyramid": pyramid})
+    torch.manual_seed(0)
+    model = OneTransModel(cfg).eval()
+    full = _batch(B=7, windows=2, seed=5)
+    user_keys = [k for k in full if k.startswith("hist_")] + ["uid", "user_counters"]
+    user = {k: full[k][:1] for k in user_keys}
+    cand = {k: full[k] for k in ("item_id", "artist_id", "album_id", "audio_embed", "item_counters",
+                                 "cross_counters")}
+    rows = dict(cand)
+    for k in user_keys:
+        rows[k] = user[k].expand(7, *user[k].shape[1:])
+    with torch.no_grad():
+        ref = model(rows)["listen_plus"]
+        got = model.score_candidates(user, cand, "listen_plus", batch_size=3)
+    torch.testing.assert_close(got, ref, rtol=1e-4, atol=1e-5)
+
+
+def test_ranking_eval_uses_kv_cache():
+    from primus_dlrm_b200.data.dataset import SyntheticEvalDataset
+    from primus_dlrm_b200.evaluation.metrics import score_candidates
+    cfg = Config.load(CONFIGS / "onetrans_tiny.yaml")
+    cfg.data.history_length = 6
+    model = OneTransModel(cfg).eval()
+    ds = SyntheticEvalDataset(cfg, num_users=2, num_items_with_history=30)
+    s = ds[0]
+    items = torch.arange(9).numpy()
+    ub = ds.user_batch(s, "cpu")
+    cb = ds.with_user_features(ds.candidate_batch(items, "cpu"), s, items, "cpu")
+    got = score_candidates(model, ub, cb, "listen_plus")
+    rows = dict(cb)
+    for k, v in ub.items():
+        rows[k] = v.expand(len(items), *v.shape[1:])
+    with torch.no_grad():
+        ref = model(rows)["listen_plus"]
+    torch.testing.assert_close(got, ref.float(), rtol=1e-4, atol=1e-5)
