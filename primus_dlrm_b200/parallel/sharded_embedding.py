@@ -26,6 +26,8 @@ Two exchange backends share the same placement and semantics:
 """
 from __future__ import annotations
 
+import os
+
 import logging
 import math
 import time
@@ -330,6 +332,10 @@ class PeerExecutor:
         self.comm_ms = 0.0
         self.time_comm = False
         self._ev: list[tuple] = []
+        # per-phase device timing of the backward (profiling aid; off by default)
+        self.time_phases = os.environ.get("PD_EXCHANGE_PHASES", "0") == "1"
+        self._phases: list[tuple[str, torch.cuda.Event]] = []
+        self.phase_ms: dict[str, float] = {}
         # map every shard of every table
         for t in emb.tables():
             shards = t.col_shards if getattr(t, "col_shards", None) else [t.shard]
@@ -382,8 +388,24 @@ class PeerExecutor:
         _native_forward(spec, ids, outs)
         self._event_end(ev)
 
+    def _mark(self, name: str) -> None:
+        if self.time_phases:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self._phases.append((name, e))
+
+    def take_phase_ms(self) -> dict[str, float]:
+        """Accumulated device time per backward phase (syncs)."""
+        if self._phases:
+            torch.cuda.synchronize()
+            for (_, a), (name, b) in zip(self._phases[:-1], self._phases[1:]):
+                self.phase_ms[name] = self.phase_ms.get(name, 0.0) + a.elapsed_time(b)
+            self._phases = []
+        return dict(self.phase_ms)
+
     def backward(self, spec: LookupSpec, ids: list[torch.Tensor], grads: list[torch.Tensor]) -> None:
         ev = self._event_pair()
+        self._mark("start")
         C = _ext.core()
         opt = spec.optimizer
         bc1, bc2 = opt.bias_corrections()
@@ -407,12 +429,15 @@ class PeerExecutor:
                 offs.append(sl.offsets if sl.offsets is not None else ids[i].new_empty(0, dtype=torch.int64))
             meta4 = torch.tensor(meta4, dtype=torch.int64)
             keys = C.emb_keys(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
+            self._mark("keys")
             ometa = torch.tensor([[int(tmeta[k, 2]), t.chunk, _KIND_CODE.get(getattr(t, "kind", "row_wise"), 0),
                                    t.owner if getattr(t, "owner", None) is not None else 0]
                                   for k, t in enumerate(tables)], dtype=torch.int64)
             comp = C.owner_keys(keys, ometa, W)
             skeys, perm = torch.sort(comp)
+            self._mark("sort")
             uniq, seg = torch.unique_consecutive(skeys, return_inverse=True)
+            self._mark("unique")
             scale = grow = None
             if any_pooled:
                 scale, grow = C.emb_pooled_scale(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
@@ -421,6 +446,7 @@ class PeerExecutor:
             C.emb_reduce_update(views, meta5, weights, ptrs, [w.new_empty(0) for w in weights],
                                 [w.new_empty(0) for w in weights], tmeta, dim, skeys, perm, scale, grow,
                                 0, 0.0, 0.0, 0.0, 0.0, 0.0, 1.0, 1.0, self.err, out_rows=reduced, seg=seg)
+            self._mark("local_reduce")
             if uniq.numel() and int(uniq[-1]) == torch.iinfo(torch.int64).max:
                 uniq, reduced = uniq[:-1], reduced[:-1]
             owner = uniq >> _OWNER_SHIFT
@@ -428,6 +454,7 @@ class PeerExecutor:
             allc = [torch.zeros_like(cnt) for _ in range(W)]
             dist.all_gather(allc, cnt, group=self.group)
             M = torch.stack(allc).cpu()                      # [src, owner 0..W]
+            self._mark("counts")
             need = [int(M[:, d].sum() + M[:, W].sum()) for d in range(W)]
             cap, kp, rp = self._recv_buffer(dim, max(need))
             dst_off = [int(M[: self.rank, d].sum()) for d in range(W)]
@@ -436,20 +463,25 @@ class PeerExecutor:
             keys_only = uniq & _KEY_MASK
             C.push_rows(keys_only, reduced.contiguous(), torch.tensor(kp), torch.tensor(rp),
                         torch.tensor(dst_off), torch.tensor(bcast_off), torch.tensor(seg_start))
+            self._mark("push")
             self.barrier()
+            self._mark("barrier")
             R = need[self.rank]
             if R:
                 buf, cap = self.recv[dim]
                 rk = buf.local[: cap * 8].view(torch.int64)[:R]
                 rr = buf.local[cap * 8: cap * 8 + cap * dim * 4].view(torch.float32).view(cap, dim)[:R]
                 sk2, perm2 = torch.sort(rk)
+                self._mark("owner_sort")
                 s1 = [t.state[0] if len(t.state) > 0 else t.weight.new_empty(0) for t in tables]
                 s2 = [t.state[1] if len(t.state) > 1 else t.weight.new_empty(0) for t in tables]
                 meta_r = torch.tensor([[0, 0, 0, -1, R]], dtype=torch.int64)
                 C.emb_reduce_update([rr], meta_r, weights, ptrs, s1, s2, tmeta, dim, sk2, perm2, None, None,
                                     opt.code, opt.lr * opt.lr_scale, opt.eps, opt.weight_decay, opt.beta1,
                                     opt.beta2, bc1, bc2, self.err)
+                self._mark("owner_update")
         self.barrier()
+        self._mark("final_barrier")
         self._event_end(ev)
 
     # -- timing ------------------------------------------------------------
