@@ -191,6 +191,9 @@ def main() -> None:
         launches += gemm.launch_count() - g0
     ms = ev0.elapsed_time(ev1) / args.steps
     a2a_ms = engine.exposed_comm_ms() / args.steps
+    phases = {}
+    if ex is not None and hasattr(ex, "take_phase_ms") and getattr(ex, "time_phases", False):
+        phases = {k: round(v / (args.steps + args.warmup), 3) for k, v in ex.take_phase_ms().items() if k != "start"}
     if ex is not None and hasattr(ex, "time_comm"):
         ex.time_comm = False
 
@@ -239,6 +242,7 @@ def main() -> None:
                                  "route/dedup/push/barrier/update) on the compute stream; 0 on 1 GPU"),
             "tflops_per_gpu": round(flops * args.per_gpu_batch / (ms / 1000.0) / 1e12, 1),
             "clocks": clocks,
+            **({"exchange_bwd_phase_ms_rank0": phases} if phases else {}),
         })
     if world > 1:
         dist.barrier()

@@ -87,7 +87,10 @@ __device__ __forceinline__ int find_slot(const int64_t* off, int n, int64_t p) {
 __device__ __forceinline__ const float* row_ptr(const Table& t, int64_t g, bool& ok) {
   ok = (g >= 0 && g < t.rows);
   if (!ok) return nullptr;
-  int64_t owner = g / t.chunk;
+  // owner = g / chunk; 32-bit division when both fit (tables below 2^32 rows)
+  int64_t owner = 0;
+  if (t.n_shards > 1)
+    owner = (g < 0xffffffffll && t.chunk < 0xffffffffll) ? int64_t(uint32_t(g) / uint32_t(t.chunk)) : g / t.chunk;
   if (owner >= t.n_shards) owner = t.n_shards - 1;
   const int64_t r = g - owner * t.chunk;
   return t.shards[owner] + r * t.dim;
@@ -96,8 +99,12 @@ __device__ __forceinline__ const float* row_ptr(const Table& t, int64_t g, bool&
 // ---------------------------------------------------------------------------
 // Unpooled gather: out[slot][i] = W[table][ids[i]]
 // Threads of a warp split into groups of `lanes` threads, each group owning a
-// row; each thread moves `vpt` float4 of the row.
+// row; each thread moves `vpt` float4 of the row. A group handles kUnroll
+// rows per iteration with all their id and row loads issued before any
+// store, so several peer (NVLink) reads are in flight per thread.
 // ---------------------------------------------------------------------------
+constexpr int kGatherUnroll = 4;
+
 template <typename IdT, typename OutT>
 __global__ void __launch_bounds__(256) gather_kernel(const __grid_constant__ GatherParams P,
                                                      int64_t total, int* err) {
@@ -110,21 +117,41 @@ __global__ void __launch_bounds__(256) gather_kernel(const __grid_constant__ Gat
   if (grp >= groups_per_warp) return;
   const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-  for (int64_t r = warp_global * groups_per_warp + grp; r < total; r += n_warps * groups_per_warp) {
-    const int s = find_slot(P.slot_off, P.n_slots, r);
-    const Slot& sl = P.slots[s];
-    const int64_t i = r - P.slot_off[s];
-    const int64_t g = load_id<IdT>(sl.ids, i);
-    bool ok;
-    const float* src = row_ptr(P.tables[sl.table], g, ok);
-    OutT* dst = static_cast<OutT*>(sl.io) + i * sl.io_stride;
-    if (!ok && sub == 0) set_error(err, kIdOutOfRange);
+  const int64_t stride = n_warps * groups_per_warp;
+  for (int64_t r0 = warp_global * groups_per_warp + grp; r0 < total; r0 += stride * kGatherUnroll) {
+    const float* src[kGatherUnroll];
+    OutT* dst[kGatherUnroll];
+    bool live[kGatherUnroll];
+#pragma unroll
+    for (int u = 0; u < kGatherUnroll; ++u) {
+      const int64_t r = r0 + u * stride;
+      live[u] = r < total;
+      src[u] = nullptr;
+      dst[u] = nullptr;
+      if (live[u]) {
+        const int s = find_slot(P.slot_off, P.n_slots, r);
+        const Slot& sl = P.slots[s];
+        const int64_t i = r - P.slot_off[s];
+        const int64_t g = load_id<IdT>(sl.ids, i);
+        bool ok;
+        src[u] = row_ptr(P.tables[sl.table], g, ok);
+        dst[u] = static_cast<OutT*>(sl.io) + i * sl.io_stride;
+        if (!ok && sub == 0) set_error(err, kIdOutOfRange);
+      }
+    }
     for (int v = sub; v < nvec; v += lanes) {
-      float4 x = ok ? __ldg(reinterpret_cast<const float4*>(src) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
-      if constexpr (std::is_same<OutT, float>::value) {
-        reinterpret_cast<float4*>(dst)[v] = x;
-      } else {
-        store4_bf16(dst + 4 * v, x);
+      float4 x[kGatherUnroll];
+#pragma unroll
+      for (int u = 0; u < kGatherUnroll; ++u)
+        x[u] = src[u] ? __ldcg(reinterpret_cast<const float4*>(src[u]) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < kGatherUnroll; ++u) {
+        if (!live[u]) continue;
+        if constexpr (std::is_same<OutT, float>::value) {
+          reinterpret_cast<float4*>(dst[u])[v] = x[u];
+        } else {
+          store4_bf16(dst[u] + 4 * v, x[u]);
+        }
       }
     }
   }

@@ -78,6 +78,10 @@ def main(argv=None) -> dict:
         out = fwd(i)
         out.backward(torch.ones_like(out))
     torch.cuda.synchronize()
+    ex = emb.executor
+    if ex is not None and hasattr(ex, "take_phase_ms"):
+        ex.take_phase_ms()
+        ex.phase_ms = {}                      # phases of the timed steps only
     if world > 1:
         dist.barrier()
     ef = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
@@ -95,7 +99,6 @@ def main(argv=None) -> dict:
     torch.cuda.synchronize()
     fwd_ms = sum(s.elapsed_time(e) for s, e in ef) / a.steps
     bwd_ms = sum(s.elapsed_time(e) for s, e in eb) / a.steps
-    ex = emb.executor
     if ex is not None and hasattr(ex, "check"):
         ex.check()
     phases = ex.take_phase_ms() if ex is not None and hasattr(ex, "take_phase_ms") else {}
@@ -126,7 +129,7 @@ def main(argv=None) -> dict:
            "fwd_frac_of_link_roofline": round(roof_f / fwd_ms, 3) if fwd_ms > 0 and world > 1 else None,
            "bwd_frac_of_link_roofline": round(roof_b / bwd_ms, 3) if bwd_ms > 0 and world > 1 else None}
     if phases:
-        res["bwd_phase_ms_rank0"] = {k: round(v / (a.steps + a.warmup), 3) for k, v in phases.items()}
+        res["bwd_phase_ms_rank0"] = {k: round(v / a.steps, 3) for k, v in phases.items() if k != "start"}
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:
