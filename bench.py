@@ -176,6 +176,9 @@ def main() -> None:
     if ex is not None and hasattr(ex, "time_comm"):
         ex.time_comm = True
         ex.take_comm_ms()
+    if ex is not None and hasattr(ex, "take_phase_ms"):
+        ex.take_phase_ms()
+        ex.phase_ms = {}                          # phases of the timed steps only
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -193,7 +196,7 @@ def main() -> None:
     a2a_ms = engine.exposed_comm_ms() / args.steps
     phases = {}
     if ex is not None and hasattr(ex, "take_phase_ms") and getattr(ex, "time_phases", False):
-        phases = {k: round(v / (args.steps + args.warmup), 3) for k, v in ex.take_phase_ms().items() if k != "start"}
+        phases = {k: round(v / args.steps, 3) for k, v in ex.take_phase_ms().items() if k != "start"}
     if ex is not None and hasattr(ex, "time_comm"):
         ex.time_comm = False
 

@@ -21,7 +21,7 @@ void emb_reduce_update(std::vector<at::Tensor>, at::Tensor, std::vector<at::Tens
 std::vector<at::Tensor> norm_fwd(at::Tensor, c10::optional<at::Tensor>, at::Tensor, c10::optional<at::Tensor>,
                                  double, int64_t);
 std::vector<at::Tensor> norm_bwd(at::Tensor, at::Tensor, c10::optional<at::Tensor>, at::Tensor, at::Tensor,
-                                 c10::optional<at::Tensor>, int64_t);
+                                 c10::optional<at::Tensor>, int64_t, int64_t);
 // loss.cu
 std::vector<at::Tensor> heads_loss_fwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, std::vector<double>,
                                        std::vector<int64_t>);
@@ -39,6 +39,7 @@ std::vector<int64_t> ipc_open(at::Tensor);
 void ipc_close(int64_t);
 void push_rows(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor);
 void signal_barrier(at::Tensor, int64_t, int64_t, int64_t, at::Tensor);
+void peer_put_row(at::Tensor, at::Tensor, int64_t);
 at::Tensor owner_keys(at::Tensor, at::Tensor, int64_t);
 void peer_reduce_slice(at::Tensor, int64_t, at::Tensor, int64_t, int64_t, double);
 void peer_gather_slices(at::Tensor, int64_t, at::Tensor, at::Tensor);
@@ -57,7 +58,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bc1"), py::arg("bc2"), py::arg("err"), py::arg("out_rows") = py::none(),
         py::arg("seg") = py::none());
   m.def("norm_fwd", &pd::norm_fwd);
-  m.def("norm_bwd", &pd::norm_bwd);
+  m.def("norm_bwd", &pd::norm_bwd, py::arg("xin"), py::arg("dy"), py::arg("dz_extra"), py::arg("w"),
+        py::arg("rstd"), py::arg("mean"), py::arg("kind"), py::arg("ex_off") = 0);
   m.def("heads_loss_fwd", &pd::heads_loss_fwd);
   m.def("heads_loss_bwd", &pd::heads_loss_bwd);
   m.def("grad_sqnorm", &pd::grad_sqnorm);
@@ -69,6 +71,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &pd::ipc_close);
   m.def("push_rows", &pd::push_rows);
   m.def("signal_barrier", &pd::signal_barrier);
+  m.def("peer_put_row", &pd::peer_put_row, "row `rank` of every rank's int64 [W, n] board = src (peer stores)");
   m.def("owner_keys", &pd::owner_keys);
   m.def("peer_reduce_slice", &pd::peer_reduce_slice, "own[a:b) = scale * sum over ranks of peer[a:b) (NVLink P2P loads)");
   m.def("peer_gather_slices", &pd::peer_gather_slices, "copy every other rank's slice from that rank (all-gather)");

@@ -141,6 +141,38 @@ void push_rows(at::Tensor keys, at::Tensor rows, at::Tensor peer_keys, at::Tenso
 }
 
 // ---------------------------------------------------------------------------
+// one small int64 row from this rank into a board on every rank
+// ---------------------------------------------------------------------------
+// Board on every rank: int64 [W, n]; this rank writes its row at index rank of
+// every peer's board (the routing counts of the sparse exchange). A signal
+// barrier after it publishes the rows.
+struct PeerRowParams {
+  int64_t* boards[64];
+  int world;
+  int rank;
+};
+
+__global__ void peer_put_row_kernel(const __grid_constant__ PeerRowParams P, const int64_t* __restrict__ src, int n) {
+  for (int d = blockIdx.x; d < P.world; d += gridDim.x)
+    for (int i = threadIdx.x; i < n; i += blockDim.x) P.boards[d][int64_t(P.rank) * n + i] = src[i];
+}
+
+void peer_put_row(at::Tensor src, at::Tensor boards, int64_t rank) {
+  const int W = int(boards.numel());
+  TORCH_CHECK(W >= 1 && W <= 64 && rank >= 0 && rank < W);
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == at::kLong && src.is_contiguous() && src.dim() == 1);
+  PeerRowParams P;
+  P.world = W;
+  P.rank = int(rank);
+  auto a = boards.accessor<int64_t, 1>();
+  for (int r = 0; r < W; ++r) P.boards[r] = reinterpret_cast<int64_t*>(static_cast<uintptr_t>(a[r]));
+  const int n = int(src.numel());
+  if (n == 0) return;
+  peer_put_row_kernel<<<W, 128, 0, stream()>>>(P, src.data_ptr<int64_t>(), n);
+  PD_CHECK_LAUNCH();
+}
+
+// ---------------------------------------------------------------------------
 // barrier over signal pads
 // ---------------------------------------------------------------------------
 struct BarrierParams {

@@ -36,7 +36,7 @@ from primus_dlrm_b200.ops.attention import (
     _native_ok as _fmha_native_ok, causal_attention_all_rows, pyramid_attention, pyramid_attention_qkv,
 )
 from primus_dlrm_b200.ops.embedding import SparseOptimizer
-from primus_dlrm_b200.ops.norm import add_norm, make_norm
+from primus_dlrm_b200.ops.norm import add_norm, make_norm, norm_with_tail
 
 
 def pyramid_schedule(l_s: int, l_ns: int, n_layers: int) -> list[int]:
@@ -137,8 +137,8 @@ class OneTransBlock(nn.Module):
     def forward(self, x: torch.Tensor, q_len: int, n_s_tokens: int) -> torch.Tensor:
         kv_len = x.shape[1]
         n_ns = kv_len - n_s_tokens
-        a = self.attn(self.norm1(x), n_s=n_s_tokens, q_len=q_len)
-        x_tail = x[:, kv_len - q_len:]
+        h, x_tail = norm_with_tail(self.norm1, x, q_len)
+        a = self.attn(h, n_s=n_s_tokens, q_len=q_len)
         y, z = add_norm(a, x_tail, self.norm2.weight,
                         getattr(self.norm2, "bias", None), self.norm2.eps, self.norm2.kind)
         fused = dense.mixed_ffn(y, z, q_len - n_ns, self.ffn.s_w1.weight, self.ffn.s_w2.weight,
@@ -273,17 +273,18 @@ class OneTransModel(BaseModel):
     def _backbone(self, batch: dict[str, torch.Tensor]):
         ot = self.config.model.transformer
         pools, scal = self._lookup(batch)
-        s_tokens = torch.cat([tok(raw) for tok, raw in zip(self.seq_tokenizers.values(), pools)], dim=1)
+        s_parts = [tok(raw) for tok, raw in zip(self.seq_tokenizers.values(), pools)]
         parts = [scal]
         for df in self.config.feature.dense_features:
             x = batch[df.name]
             parts.append(self.dense_projs[df.name](x) if df.name in self.dense_projs else x.to(scal.dtype))
         ns_raw = torch.cat([p.to(scal.dtype) for p in parts], dim=-1)
         ns_tokens = self.ns_tokenizer(ns_raw)
-        x = torch.cat([s_tokens, ns_tokens.to(s_tokens.dtype)], dim=1)
+        # one concatenation of every S pool's tokens and the NS tokens
+        x = torch.cat(s_parts + [ns_tokens.to(s_parts[0].dtype)], dim=1)
         B = x.shape[0]
         L_NS = ot.n_ns_tokens
-        L_S = s_tokens.shape[1]
+        L_S = x.shape[1] - L_NS
         sched = pyramid_schedule(L_S, L_NS, ot.n_layers) if ot.use_pyramid else [L_S] * ot.n_layers
         for l, block in enumerate(self.blocks):
             q_len = sched[l] + L_NS

@@ -81,9 +81,11 @@ def _dw(dy, x, n_s, wdt):
     the first n_s rows of every sample, per-token NS weights."""
     B, T, N = dy.shape
     K = x.shape[-1]
-    dws = torch.matmul(dy.reshape(-1, N).t(), x.reshape(-1, K)).float()
+    # fp32 results straight from the GEMM (no bf16 round trip, no cast kernel)
+    dws = torch.mm(dy.reshape(-1, N).t(), x.reshape(-1, K), out_dtype=torch.float32)
     if T > n_s:
-        dwn = torch.einsum("btm,btn->tmn", dy[:, n_s:], x[:, n_s:]).float()
+        # one GEMM per NS token over the batch: [N, B] x [B, K] views, no copies
+        dwn = torch.bmm(dy[:, n_s:].permute(1, 2, 0), x[:, n_s:].transpose(0, 1), out_dtype=torch.float32)
         dws -= dwn.sum(0)
     else:
         dwn = torch.zeros(0, N, K, device=dy.device)
@@ -274,9 +276,9 @@ class _MLP2Native(torch.autograd.Function):
         dp = dpre.reshape(rows, F_)
         dw2 = torch.matmul(d2.t(), h.reshape(rows, F_)).to(dt_w2)
         dw1 = torch.matmul(dp.t(), xb.reshape(rows, K)).to(dt_w1)
-        dpos = dout.float().sum(0)                      # [L, N]
+        dpos = dout.sum(0, dtype=torch.float32)         # [L, N], fp32 accumulation without an fp32 copy
         db2 = dpos.sum(0).to(dt_b2)
-        db1 = dp.float().sum(0).to(dt_b1)
+        db1 = dp.sum(0, dtype=torch.float32).to(dt_b1)
         return dx, dw1, db1, dw2, db2, (dpos.to(dt_add) if has_add else None)
 
 

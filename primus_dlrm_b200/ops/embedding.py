@@ -339,8 +339,9 @@ class GroupedLookup(torch.autograd.Function):
     def forward(ctx, anchor, spec: LookupSpec, *ids):
         dev = spec.err.device if spec.err is not None else spec.tables[0].weight.device
         outs = [torch.empty(shape, dtype=spec.dtype, device=dev) for shape in spec.group_shapes]
+        plan = None
         if spec.executor is not None:
-            spec.executor.forward(spec, list(ids), outs)
+            plan = spec.executor.forward(spec, list(ids), outs, backward=not isinstance(ctx, _NoCtx))
         elif spec.native:
             _native_forward(spec, list(ids), outs)
         else:
@@ -352,6 +353,7 @@ class GroupedLookup(torch.autograd.Function):
                 else:
                     view.copy_(_eager_rows(t, ids[i].reshape(-1)))
         ctx.spec = spec
+        ctx.exchange_plan = plan
         ctx.save_for_backward(*ids)
         return tuple(outs)
 
@@ -367,7 +369,8 @@ class GroupedLookup(torch.autograd.Function):
         spec.optimizer.step += 1
         with torch.no_grad():
             if spec.executor is not None:
-                spec.executor.backward(spec, ids, gs)
+                spec.executor.backward(spec, ids, gs, plan=ctx.exchange_plan)
+                ctx.exchange_plan = None
             elif spec.native:
                 _native_backward(spec, ids, gs)
             else:
@@ -383,5 +386,7 @@ def grouped_lookup(spec: LookupSpec, ids: list[torch.Tensor], anchor: torch.Tens
 
 
 class _NoCtx:
+    exchange_plan = None
+
     def save_for_backward(self, *a):
         pass

@@ -57,6 +57,43 @@ class _NormFn(torch.autograd.Function):
         return (dx, dx if ctx.fused else None, dw, db if ctx.has_bias else None, None, None)
 
 
+class _NormTailFn(torch.autograd.Function):
+    """``(norm(x), x[:, T - q:])`` as one autograd node.  A pre-norm block
+    normalises all T rows of its input but carries only the last q rows on as
+    the residual; with the slice taken here its gradient is added inside the
+    norm backward kernel, so no zero-filled [B, T, D] gradient of the slice and
+    no separate add are materialised."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps: float, kind: int, q_len: int):
+        C = _ext.core()
+        xc = x if x.is_contiguous() else x.contiguous()
+        y, _, rstd, mean = C.norm_fwd(xc, None, weight, bias, eps, kind)
+        T = x.shape[1]
+        ctx.kind, ctx.has_bias, ctx.off = kind, bias is not None, T - q_len
+        ctx.save_for_backward(xc, weight, rstd, mean if kind == 1 else rstd)
+        return y, x[:, T - q_len:]
+
+    @staticmethod
+    def backward(ctx, dy, dtail):
+        C = _ext.core()
+        xin, weight, rstd, mean = ctx.saved_tensors
+        if dy is None:
+            dy = torch.zeros_like(xin)
+        ex = dtail.to(torch.bfloat16) if dtail is not None else None
+        dx, dw, db = C.norm_bwd(xin, dy.to(torch.bfloat16), ex, weight, rstd,
+                                mean if ctx.kind == 1 else None, ctx.kind, ctx.off if ex is not None else 0)
+        return dx, dw, db if ctx.has_bias else None, None, None, None
+
+
+def norm_with_tail(norm: nn.Module, x: torch.Tensor, q_len: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(norm(x), x[:, T - q_len:]) for x [B, T, D]; one fused backward when native."""
+    T = x.shape[1]
+    if _use_native(x) and x.dim() == 3 and 0 < q_len <= T:
+        return _NormTailFn.apply(x, norm.weight, getattr(norm, "bias", None), norm.eps, norm.kind, q_len)
+    return norm(x), x[:, T - q_len:]
+
+
 def rms_norm_ref(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     rms = x.float().pow(2).mean(-1, keepdim=True).add(eps).rsqrt()
     return (x.float() * rms).to(x.dtype) * weight

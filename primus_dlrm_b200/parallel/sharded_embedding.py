@@ -174,7 +174,8 @@ class A2AExecutor:
         dist.all_to_all_single(out, x.contiguous(), recv, send, group=self.group)
         return out
 
-    def forward(self, spec: LookupSpec, ids: list[torch.Tensor], outs: list[torch.Tensor]) -> None:
+    def forward(self, spec: LookupSpec, ids: list[torch.Tensor], outs: list[torch.Tensor],
+                backward: bool = False) -> None:
         spec.saved = {}
         for dim, sidx in _by_dim(spec).items():
             keys, owners, slot_of, gl = [], [], [], []
@@ -216,7 +217,7 @@ class A2AExecutor:
                 off += n
             spec.saved[dim] = (perm, send_l, recv_l, r_keys, r_tab)
 
-    def backward(self, spec: LookupSpec, ids: list[torch.Tensor], grads: list[torch.Tensor]) -> None:
+    def backward(self, spec: LookupSpec, ids: list[torch.Tensor], grads: list[torch.Tensor], plan=None) -> None:
         for dim, sidx in _by_dim(spec).items():
             perm, send_l, recv_l, r_keys, r_tab = spec.saved[dim]
             rows, keep_all = [], []
@@ -321,6 +322,26 @@ def exchange_pointers(t: torch.Tensor, rank: int, world: int, group, opened: lis
     return ptrs
 
 
+_PLAN_DIMS = 8   # distinct embedding dims one lookup may route
+
+
+class _DimPlan:
+    """Backward routing of the slots of one embedding dim (see ``PeerExecutor._plan``)."""
+
+    def __init__(self, dim, sidx, tables, weights, ptrs, tmeta, meta5, skeys, perm, seg, uniq, scale, grow):
+        self.dim, self.sidx, self.tables, self.weights, self.ptrs = dim, sidx, tables, weights, ptrs
+        self.tmeta, self.meta5 = tmeta, meta5
+        self.skeys, self.perm, self.seg, self.uniq = skeys, perm, seg, uniq
+        self.scale, self.grow = scale, grow
+
+
+class _Plan:
+    def __init__(self):
+        self.dims: list[_DimPlan] = []
+        self.host: torch.Tensor | None = None
+        self.event: torch.cuda.Event | None = None
+
+
 class PeerExecutor:
     def __init__(self, emb, rank: int, world: int, device: torch.device, group=None,
                  barrier_timeout_s: float = 30.0):
@@ -352,6 +373,15 @@ class PeerExecutor:
         self.pads = SymmetricBuffer(64 * 8, device, rank, world, group)
         self.pad_ptrs = torch.tensor(self.pads.ptrs, dtype=torch.int64)
         self.recv: dict[int, tuple[SymmetricBuffer, int]] = {}
+        # routing plan of the backward, made during the forward on a side
+        # stream: its own signal pads (epochs independent of the main
+        # stream's barriers) and a count board int64 [W, _PLAN_DIMS * (W + 2)]
+        self.plan_epoch = 0
+        self.plan_row = _PLAN_DIMS * (world + 2)
+        self.plan_buf = SymmetricBuffer(64 * 8 + world * self.plan_row * 8, device, rank, world, group)
+        self.plan_pads = torch.tensor(self.plan_buf.ptrs, dtype=torch.int64)
+        self.plan_boards = torch.tensor([p + 64 * 8 if p else 0 for p in self.plan_buf.ptrs], dtype=torch.int64)
+        self.side = torch.cuda.Stream(device)
         self.barrier()
 
     # -- primitives --------------------------------------------------------
@@ -383,10 +413,89 @@ class PeerExecutor:
         return cap, kp, rp
 
     # -- lookup ------------------------------------------------------------
-    def forward(self, spec: LookupSpec, ids: list[torch.Tensor], outs: list[torch.Tensor]) -> None:
+    def forward(self, spec: LookupSpec, ids: list[torch.Tensor], outs: list[torch.Tensor],
+                backward: bool = False) -> "_Plan | None":
+        """Gather every slot (peer loads from the owners).  With ``backward``
+        the routing of the coming backward is planned as well, on a side
+        stream that overlaps the forward: it needs the ids only."""
         ev = self._event_pair()
         _native_forward(spec, ids, outs)
         self._event_end(ev)
+        return self._plan(spec, ids, outs) if backward else None
+
+    def _plan(self, spec: LookupSpec, ids: list[torch.Tensor], outs: list[torch.Tensor]) -> "_Plan":
+        """Owner-sorted keys, their permutation, the unique-row segment of
+        every key and per-owner unique counts of every rank (exchanged through
+        a peer-memory board, copied to pinned host memory).  The backward then
+        runs without a host synchronisation: it waits on this plan's event,
+        which completed long before, instead of draining the compute stream."""
+        C = _ext.core()
+        W = self.world
+        main = torch.cuda.current_stream(self.device)
+        side = self.side
+        side.wait_stream(main)
+        groups = list(_by_dim(spec).items())
+        if len(groups) > _PLAN_DIMS:
+            raise RuntimeError(f"peer exchange plans at most {_PLAN_DIMS} embedding dims, got {len(groups)}")
+        plan = _Plan()
+        with torch.cuda.stream(side):
+            cnts = []
+            for dim, sidx in groups:
+                tables, remap = _launch_tables(spec, sidx)
+                weights = [t.weight for t in tables]
+                ptrs = [t.device_ptrs() for t in tables]
+                tmeta = _table_meta(tables)
+                slot_ids = [ids[i].reshape(-1) for i in sidx]
+                views, meta4, offs, any_pooled = [], [], [], False
+                for i in sidx:
+                    sl = spec.slots[i]
+                    views.append(_slot_view(outs[sl.group], sl.col, dim))
+                    L = 0
+                    if sl.pool:
+                        any_pooled = True
+                        nb = outs[sl.group].numel() // outs[sl.group].shape[-1]
+                        L = ids[i].numel() // max(nb, 1) if sl.offsets is None else 0
+                    meta4.append([remap[sl.table], sl.pool, L, sl.pad_id])
+                    offs.append(sl.offsets if sl.offsets is not None else ids[i].new_empty(0, dtype=torch.int64))
+                meta4 = torch.tensor(meta4, dtype=torch.int64)
+                keys = C.emb_keys(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
+                ometa = torch.tensor([[int(tmeta[k, 2]), t.chunk, _KIND_CODE.get(getattr(t, "kind", "row_wise"), 0),
+                                       t.owner if getattr(t, "owner", None) is not None else 0]
+                                      for k, t in enumerate(tables)], dtype=torch.int64)
+                skeys, perm = torch.sort(C.owner_keys(keys, ometa, W))
+                n = skeys.numel()
+                first = torch.ones(n, dtype=torch.bool, device=self.device)
+                if n > 1:
+                    torch.ne(skeys[1:], skeys[:-1], out=first[1:])
+                seg = torch.cumsum(first, 0) - 1
+                # owner W = replicated tables, W + 1 = padding keys (dropped)
+                own = (skeys >> _OWNER_SHIFT).clamp_(max=W + 1)
+                cnt = torch.zeros(W + 2, dtype=torch.int64, device=self.device).index_add_(0, own, first.long())
+                uniq = torch.empty(n, dtype=torch.int64, device=self.device).scatter_(0, seg, skeys & _KEY_MASK)
+                scale = grow = None
+                if any_pooled:
+                    scale, grow = C.emb_pooled_scale(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
+                meta5 = torch.cat([meta4, torch.tensor([[x.numel()] for x in slot_ids], dtype=torch.int64)], 1)
+                plan.dims.append(_DimPlan(dim, sidx, tables, weights, ptrs, tmeta, meta5, skeys, perm, seg, uniq,
+                                          scale, grow))
+                cnts.append(cnt)
+            row = torch.zeros(self.plan_row, dtype=torch.int64, device=self.device)
+            row[: len(cnts) * (W + 2)] = torch.cat(cnts)
+            C.peer_put_row(row, self.plan_boards, self.rank)
+            self.plan_epoch += 1
+            C.signal_barrier(self.plan_pads, self.rank, self.plan_epoch, self.timeout_ns, self.err)
+            board = self.plan_buf.local[64 * 8:].view(torch.int64)[: W * self.plan_row]
+            plan.host = torch.empty(W * self.plan_row, dtype=torch.int64, pin_memory=True)
+            plan.host.copy_(board, non_blocking=True)
+            plan.event = torch.cuda.Event()
+            plan.event.record(side)
+        for d in plan.dims:
+            for t in (d.skeys, d.perm, d.seg, d.uniq, d.scale, d.grow):
+                if t is not None:
+                    t.record_stream(main)
+        for t in ids:
+            t.record_stream(side)
+        return plan
 
     def _mark(self, name: str) -> None:
         if self.time_phases:
@@ -403,65 +512,40 @@ class PeerExecutor:
             self._phases = []
         return dict(self.phase_ms)
 
-    def backward(self, spec: LookupSpec, ids: list[torch.Tensor], grads: list[torch.Tensor]) -> None:
+    def backward(self, spec: LookupSpec, ids: list[torch.Tensor], grads: list[torch.Tensor],
+                 plan: "_Plan | None" = None) -> None:
+        """Local reduction per unique row, push to the owners, owner update.
+        Without a plan from the forward (a lookup run outside autograd) the
+        plan is made here."""
+        if plan is None:
+            plan = self._plan(spec, ids, grads)
         ev = self._event_pair()
         self._mark("start")
         C = _ext.core()
         opt = spec.optimizer
         bc1, bc2 = opt.bias_corrections()
         W = self.world
-        for dim, sidx in _by_dim(spec).items():
-            tables, remap = _launch_tables(spec, sidx)
-            weights = [t.weight for t in tables]
-            ptrs = [t.device_ptrs() for t in tables]
-            tmeta = _table_meta(tables)
-            slot_ids = [ids[i].reshape(-1) for i in sidx]
-            views, meta4, offs, any_pooled = [], [], [], False
-            for i in sidx:
-                sl = spec.slots[i]
-                views.append(_slot_view(grads[sl.group], sl.col, dim))
-                L = 0
-                if sl.pool:
-                    any_pooled = True
-                    nb = grads[sl.group].numel() // grads[sl.group].shape[-1]
-                    L = ids[i].numel() // max(nb, 1) if sl.offsets is None else 0
-                meta4.append([remap[sl.table], sl.pool, L, sl.pad_id])
-                offs.append(sl.offsets if sl.offsets is not None else ids[i].new_empty(0, dtype=torch.int64))
-            meta4 = torch.tensor(meta4, dtype=torch.int64)
-            keys = C.emb_keys(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
-            self._mark("keys")
-            ometa = torch.tensor([[int(tmeta[k, 2]), t.chunk, _KIND_CODE.get(getattr(t, "kind", "row_wise"), 0),
-                                   t.owner if getattr(t, "owner", None) is not None else 0]
-                                  for k, t in enumerate(tables)], dtype=torch.int64)
-            comp = C.owner_keys(keys, ometa, W)
-            skeys, perm = torch.sort(comp)
-            self._mark("sort")
-            uniq, seg = torch.unique_consecutive(skeys, return_inverse=True)
-            self._mark("unique")
-            scale = grow = None
-            if any_pooled:
-                scale, grow = C.emb_pooled_scale(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
-            reduced = torch.empty(uniq.numel(), dim, dtype=torch.float32, device=keys.device)
-            meta5 = torch.cat([meta4, torch.tensor([[s.numel()] for s in slot_ids], dtype=torch.int64)], 1)
-            C.emb_reduce_update(views, meta5, weights, ptrs, [w.new_empty(0) for w in weights],
-                                [w.new_empty(0) for w in weights], tmeta, dim, skeys, perm, scale, grow,
-                                0, 0.0, 0.0, 0.0, 0.0, 0.0, 1.0, 1.0, self.err, out_rows=reduced, seg=seg)
+        main = torch.cuda.current_stream(self.device)
+        main.wait_event(plan.event)
+        plan.event.synchronize()                  # finished during the forward: no drain of the compute stream
+        board = plan.host.view(W, self.plan_row)
+        for di, d in enumerate(plan.dims):
+            dim = d.dim
+            M = board[:, di * (W + 2): di * (W + 2) + W + 1]   # [src, owner 0..W] unique counts
+            U = int(M[self.rank].sum())
+            views = [_slot_view(grads[spec.slots[i].group], spec.slots[i].col, dim) for i in d.sidx]
+            reduced = torch.empty(U + 1, dim, dtype=torch.float32, device=self.device)  # + the padding run
+            C.emb_reduce_update(views, d.meta5, d.weights, d.ptrs, [w.new_empty(0) for w in d.weights],
+                                [w.new_empty(0) for w in d.weights], d.tmeta, dim, d.skeys, d.perm, d.scale,
+                                d.grow, 0, 0.0, 0.0, 0.0, 0.0, 0.0, 1.0, 1.0, self.err, out_rows=reduced, seg=d.seg)
             self._mark("local_reduce")
-            if uniq.numel() and int(uniq[-1]) == torch.iinfo(torch.int64).max:
-                uniq, reduced = uniq[:-1], reduced[:-1]
-            owner = uniq >> _OWNER_SHIFT
-            cnt = torch.bincount(owner, minlength=W + 1)[: W + 1]
-            allc = [torch.zeros_like(cnt) for _ in range(W)]
-            dist.all_gather(allc, cnt, group=self.group)
-            M = torch.stack(allc).cpu()                      # [src, owner 0..W]
-            self._mark("counts")
-            need = [int(M[:, d].sum() + M[:, W].sum()) for d in range(W)]
+            col = M.sum(0)
+            need = [int(col[o] + col[W]) for o in range(W)]
             cap, kp, rp = self._recv_buffer(dim, max(need))
-            dst_off = [int(M[: self.rank, d].sum()) for d in range(W)]
-            bcast_off = [int(M[:, d].sum() + M[: self.rank, W].sum()) for d in range(W)]
+            dst_off = [int(M[: self.rank, o].sum()) for o in range(W)]
+            bcast_off = [int(col[o] + M[: self.rank, W].sum()) for o in range(W)]
             seg_start = [0] + torch.cumsum(M[self.rank], 0).tolist()
-            keys_only = uniq & _KEY_MASK
-            C.push_rows(keys_only, reduced.contiguous(), torch.tensor(kp), torch.tensor(rp),
+            C.push_rows(d.uniq[:U], reduced[:U], torch.tensor(kp), torch.tensor(rp),
                         torch.tensor(dst_off), torch.tensor(bcast_off), torch.tensor(seg_start))
             self._mark("push")
             self.barrier()
@@ -473,10 +557,10 @@ class PeerExecutor:
                 rr = buf.local[cap * 8: cap * 8 + cap * dim * 4].view(torch.float32).view(cap, dim)[:R]
                 sk2, perm2 = torch.sort(rk)
                 self._mark("owner_sort")
-                s1 = [t.state[0] if len(t.state) > 0 else t.weight.new_empty(0) for t in tables]
-                s2 = [t.state[1] if len(t.state) > 1 else t.weight.new_empty(0) for t in tables]
+                s1 = [t.state[0] if len(t.state) > 0 else t.weight.new_empty(0) for t in d.tables]
+                s2 = [t.state[1] if len(t.state) > 1 else t.weight.new_empty(0) for t in d.tables]
                 meta_r = torch.tensor([[0, 0, 0, -1, R]], dtype=torch.int64)
-                C.emb_reduce_update([rr], meta_r, weights, ptrs, s1, s2, tmeta, dim, sk2, perm2, None, None,
+                C.emb_reduce_update([rr], meta_r, d.weights, d.ptrs, s1, s2, d.tmeta, dim, sk2, perm2, None, None,
                                     opt.code, opt.lr * opt.lr_scale, opt.eps, opt.weight_decay, opt.beta1,
                                     opt.beta2, bc1, bc2, self.err)
                 self._mark("owner_update")

@@ -11,9 +11,12 @@
   covered by the union of compute-kernel intervals on the same device;
 * ``gemm_report`` -- (M, N, K) of GEMM kernels from the CPU op that launched
   them (matched by the trace's correlation / External id) and achieved TF/s;
+* ``idle_gaps`` -- stretches where a device runs no kernel at all, with the
+  host op that was running when each began (launch-bound or host-synchronised
+  regions of a step);
 * ``stitch`` -- merge per-rank traces into one file with per-rank process ids.
 
-CLI: ``python -m primus_dlrm_b200.training.trace_analysis {breakdown,comms,gemm,stitch} ...``
+CLI: ``python -m primus_dlrm_b200.training.trace_analysis {breakdown,comms,gemm,gaps,stitch} ...``
 """
 from __future__ import annotations
 
@@ -241,12 +244,50 @@ def stitch(paths: list[str | Path], out: str | Path) -> Path:
     return out
 
 
+def idle_gaps(trace: dict, min_us: float = 20.0, top: int = 30) -> dict:
+    """Device idle gaps (no kernel, copy or memset on any stream) longer than
+    ``min_us``, per device, with the innermost host op running at each gap's
+    start.  Totals cover the span from the first to the last device event."""
+    ev = _events(trace)
+    by_dev: dict = defaultdict(list)
+    for e in ev:
+        if _is_kernel(e):
+            dev = (e.get("args") or {}).get("device", e.get("pid"))
+            by_dev[dev].append((float(e["ts"]), float(e["ts"]) + float(e.get("dur", 0.0))))
+    host = sorted((float(e["ts"]), float(e["ts"]) + float(e.get("dur", 0.0)), e.get("name", ""))
+                  for e in ev if e.get("ph") == "X" and str(e.get("cat", "")).lower() in ("cpu_op", "user_annotation"))
+
+    def host_op(t: float) -> str:
+        best, best_len = "", float("inf")
+        for a, b, n in host:          # innermost op that contains t
+            if a > t:
+                break
+            if b >= t and b - a < best_len:
+                best, best_len = n, b - a
+        return best
+
+    out = {}
+    for dev, iv in by_dev.items():
+        m = _merge(iv)
+        gaps = [(m[i][1], m[i + 1][0]) for i in range(len(m) - 1) if m[i + 1][0] - m[i][1] >= min_us]
+        span = m[-1][1] - m[0][0] if m else 0.0
+        idle = sum(b - a for a, b in gaps)
+        rows = sorted(gaps, key=lambda g: g[0] - g[1])[:top]
+        out[str(dev)] = {
+            "span_ms": round(span / 1000, 3), "idle_ms": round(idle / 1000, 3), "n_gaps": len(gaps),
+            "top": [{"start_us": round(a - m[0][0], 1), "gap_us": round(b - a, 1), "host_op": host_op(a)}
+                    for a, b in rows],
+        }
+    return out
+
+
 def main(argv=None) -> None:
     p = argparse.ArgumentParser(description="Analyse torch.profiler Chrome traces")
     sub = p.add_subparsers(dest="cmd", required=True)
     b = sub.add_parser("breakdown"); b.add_argument("trace"); b.add_argument("--steps", type=int, default=1)
     c = sub.add_parser("comms"); c.add_argument("trace"); c.add_argument("--world-size", type=int, default=0)
     g = sub.add_parser("gemm"); g.add_argument("trace"); g.add_argument("--top", type=int, default=30)
+    i = sub.add_parser("gaps"); i.add_argument("trace"); i.add_argument("--min-us", type=float, default=20.0)
     s = sub.add_parser("stitch"); s.add_argument("traces", nargs="+"); s.add_argument("--out", required=True)
     a = p.parse_args(argv)
     if a.cmd == "breakdown":
@@ -255,6 +296,8 @@ def main(argv=None) -> None:
         res = comm_report(load_trace(a.trace), a.world_size)
     elif a.cmd == "gemm":
         res = gemm_report(load_trace(a.trace), a.top)
+    elif a.cmd == "gaps":
+        res = idle_gaps(load_trace(a.trace), a.min_us)
     else:
         res = str(stitch(a.traces, a.out))
     print(json.dumps(res, indent=1))

@@ -130,7 +130,7 @@ def test_out_of_range_id_sets_error_word():
     assert float(out[0][2].abs().sum()) == 0.0
 
 
-@pytest.mark.parametrize("D", [64, 256, 384, 1024])
+@pytest.mark.parametrize("D", [64, 256, 384, 1024, 2048])
 @pytest.mark.parametrize("kind", [0, 1])
 def test_norm_fwd_bwd(D, kind):
     from primus_dlrm_b200.ops.norm import _NormFn
@@ -164,6 +164,71 @@ def test_add_norm_fused():
     torch.testing.assert_close(z.float(), zr.to(torch.bfloat16).float())
     (y.float().sum() + 2 * z.float().sum()).backward()
     assert a.grad is not None and torch.equal(a.grad, b.grad)
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+@pytest.mark.parametrize("D", [256, 384])
+def test_add_norm_matches_fp32_reference(kind, D):
+    """Fused residual add + norm over a token-sliced (batch-strided) input with
+    an odd row count; gradients through both y and z."""
+    from primus_dlrm_b200.ops.norm import add_norm
+    torch.manual_seed(kind * 7 + D)
+    full = torch.randn(3, 45, D, device=DEV).to(torch.bfloat16)
+    a = full[:, 6:, :].detach().requires_grad_(True)          # [3, 39, D], batch stride 45 * D
+    b = torch.randn(3, 39, D, device=DEV).to(torch.bfloat16).requires_grad_(True)
+    w = (torch.rand(D, device=DEV) + 0.5).requires_grad_(True)
+    bias = torch.randn(D, device=DEV).requires_grad_(True) if kind else None
+    y, z = add_norm(a, b, w, bias, 1e-6, kind)
+    af, bf_ = a.detach().float().requires_grad_(True), b.detach().float().requires_grad_(True)
+    wf = w.detach().clone().requires_grad_(True)
+    biasf = bias.detach().clone().requires_grad_(True) if kind else None
+    zf = af + bf_
+    if kind == 0:
+        yf = zf * torch.rsqrt(zf.pow(2).mean(-1, keepdim=True) + 1e-6) * wf
+    else:
+        yf = torch.nn.functional.layer_norm(zf, (D,), wf, biasf, 1e-6)
+    torch.testing.assert_close(z.float(), zf.to(torch.bfloat16).float())
+    torch.testing.assert_close(y.float(), yf, rtol=2e-2, atol=3e-2)
+    gy = torch.randn_like(yf).to(torch.bfloat16)
+    gz = torch.randn_like(zf).to(torch.bfloat16)
+    torch.autograd.backward([y, z], [gy, gz])
+    torch.autograd.backward([yf, zf], [gy.float(), gz.float()])
+    torch.testing.assert_close(a.grad.float(), af.grad, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(b.grad.float(), bf_.grad, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(w.grad, wf.grad, rtol=2e-2, atol=1e-1)
+    if kind:
+        torch.testing.assert_close(bias.grad, biasf.grad, rtol=2e-2, atol=1e-1)
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+@pytest.mark.parametrize("q_len", [40, 17, 5])
+def test_norm_with_tail_gradient(kind, q_len):
+    """(norm(x), x[:, T-q:]) in one node: the tail's gradient is added inside
+    the norm backward; compared with the fp32 autograd of the same graph."""
+    from primus_dlrm_b200.ops.norm import make_norm, norm_with_tail
+    torch.manual_seed(q_len + kind)
+    D, T = 256, 40
+    norm = make_norm("rmsnorm" if kind == 0 else "layernorm", D).to(DEV)
+    with torch.no_grad():
+        norm.weight.uniform_(0.5, 1.5)
+        if kind:
+            norm.bias.normal_()
+    x = torch.randn(3, T, D, device=DEV).to(torch.bfloat16).requires_grad_(True)
+    y, tail = norm_with_tail(norm, x, q_len)
+    assert tail.shape == (3, q_len, D) and torch.equal(tail, x[:, T - q_len:])
+    gy = torch.randn(3, T, D, device=DEV).to(torch.bfloat16)
+    gt = torch.randn(3, q_len, D, device=DEV).to(torch.bfloat16)
+    torch.autograd.backward([y, tail * 1.0], [gy, gt])
+    xf = x.detach().float().requires_grad_(True)
+    wf = norm.weight.detach().clone().requires_grad_(True)
+    if kind == 0:
+        yf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + norm.eps) * wf
+    else:
+        yf = torch.nn.functional.layer_norm(xf, (D,), wf, norm.bias.detach(), norm.eps)
+    torch.autograd.backward([yf, xf[:, T - q_len:]], [gy.float(), gt.float()])
+    torch.testing.assert_close(y.float(), yf, rtol=2e-2, atol=3e-2)
+    torch.testing.assert_close(x.grad.float(), xf.grad, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(norm.weight.grad, wf.grad, rtol=2e-2, atol=1e-1)
 
 
 def test_heads_loss():

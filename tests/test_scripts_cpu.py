@@ -64,6 +64,20 @@ def test_trace_breakdown_comms_gemm(tmp_path):
     assert g[0]["tflops"] == pytest.approx(2 * 1024 * 256 * 512 / 100e-6 / 1e12, rel=1e-2)
 
 
+def test_idle_gaps():
+    from primus_dlrm_b200.training.trace_analysis import idle_gaps
+    tr = _trace()
+    # device 0 busy [0, 200) through the all-reduce; add a kernel at [300, 310) after a host sync
+    tr["traceEvents"].append({"ph": "X", "cat": "kernel", "name": "k", "pid": 0, "tid": 7, "ts": 300, "dur": 10,
+                              "args": {"device": 0}})
+    tr["traceEvents"].append({"ph": "X", "cat": "cpu_op", "name": "aten::item", "pid": 1, "tid": 1, "ts": 190,
+                              "dur": 100, "args": {}})
+    g = idle_gaps(tr, min_us=20)["0"]
+    assert g["n_gaps"] == 1 and g["idle_ms"] == pytest.approx(0.1)
+    assert g["top"][0]["host_op"] == "aten::item" and g["top"][0]["start_us"] == pytest.approx(200)
+    assert g["span_ms"] == pytest.approx(0.31)
+
+
 def test_stitch_traces(tmp_path):
     from primus_dlrm_b200.training.trace_analysis import stitch
     paths = []
