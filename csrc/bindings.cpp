@@ -7,6 +7,9 @@ void emb_gather(std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, st
                 std::vector<at::Tensor>, at::Tensor, int64_t, at::Tensor);
 void emb_pooled(std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, std::vector<at::Tensor>,
                 std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, int64_t, at::Tensor);
+void emb_gather_planned(std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, std::vector<at::Tensor>,
+                        std::vector<at::Tensor>, at::Tensor, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor,
+                        at::Tensor);
 at::Tensor emb_keys(std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, std::vector<at::Tensor>,
                     std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, int64_t);
 std::vector<at::Tensor> emb_pooled_scale(std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor,
@@ -50,6 +53,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("emb_gather", &pd::emb_gather);
   m.def("emb_pooled", &pd::emb_pooled);
   m.def("emb_keys", &pd::emb_keys);
+  m.def("emb_gather_planned", &pd::emb_gather_planned,
+        "deduplicated gather from an owner-sorted routing plan (unique rows once, then expanded)");
   m.def("emb_pooled_scale", &pd::emb_pooled_scale);
   m.def("emb_reduce_update", &pd::emb_reduce_update, py::arg("grads"), py::arg("slot_meta"), py::arg("weights"),
         py::arg("shard_ptrs"), py::arg("state1"), py::arg("state2"), py::arg("table_meta"), py::arg("dim"),

@@ -158,6 +158,117 @@ __global__ void __launch_bounds__(256) gather_kernel(const __grid_constant__ Gat
 }
 
 // ---------------------------------------------------------------------------
+// Deduplicated gather for sharded tables. The lookup's (table, row) keys,
+// sorted by owner and row (the same sort the backward uses), are fetched once
+// per unique key into a staging buffer -- peer reads walk each owner's shard
+// in ascending address order and a hot Zipf row crosses NVLink once -- and
+// then expanded to every position. The unique count is read on the device
+// (seg of the last sorted key + 1), so nothing waits for the host.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ const float* key_row(const GatherParams& P, int64_t key, bool& ok) {
+  int t = 0;
+  while (t + 1 < P.n_tables && P.tables[t + 1].key_base <= key) ++t;
+  const Table& T = P.tables[t];
+  return row_ptr(T, key - T.key_base, ok);
+}
+
+template <typename OutT>
+__global__ void __launch_bounds__(256) gather_unique_kernel(const __grid_constant__ GatherParams P,
+                                                            const int64_t* __restrict__ uniq,
+                                                            const int64_t* __restrict__ seg, int64_t n,
+                                                            OutT* __restrict__ stage) {
+  const int64_t U = seg[n - 1] + 1;
+  const int nvec = P.dim >> 2;
+  const int lanes = nvec < 32 ? nvec : 32;
+  const int groups_per_warp = 32 / lanes;
+  const int lane = threadIdx.x & 31;
+  const int grp = lane / lanes;
+  const int sub = lane % lanes;
+  if (grp >= groups_per_warp) return;
+  const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  const int64_t stride = n_warps * groups_per_warp;
+  for (int64_t u0 = warp_global * groups_per_warp + grp; u0 < U; u0 += stride * kGatherUnroll) {
+    const float* src[kGatherUnroll];
+#pragma unroll
+    for (int u = 0; u < kGatherUnroll; ++u) {
+      const int64_t r = u0 + u * stride;
+      src[u] = nullptr;
+      if (r < U) {
+        bool ok;
+        src[u] = key_row(P, uniq[r], ok);   // the padding key resolves to no row: zeros
+      }
+    }
+    for (int v = sub; v < nvec; v += lanes) {
+      float4 x[kGatherUnroll];
+#pragma unroll
+      for (int u = 0; u < kGatherUnroll; ++u)
+        x[u] = src[u] ? __ldcg(reinterpret_cast<const float4*>(src[u]) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < kGatherUnroll; ++u) {
+        const int64_t r = u0 + u * stride;
+        if (r >= U) continue;
+        OutT* dst = stage + r * P.dim;
+        if constexpr (std::is_same<OutT, float>::value) {
+          reinterpret_cast<float4*>(dst)[v] = x[u];
+        } else {
+          store4_bf16(dst + 4 * v, x[u]);
+        }
+      }
+    }
+  }
+}
+
+// out[perm[p]] = stage[seg[p]]: a group of threads per sorted position, rows
+// moved as 16-byte vectors, kGatherUnroll positions in flight per group.
+template <typename OutT>
+__global__ void __launch_bounds__(256) expand_kernel(const __grid_constant__ GatherParams P,
+                                                     const OutT* __restrict__ stage,
+                                                     const int64_t* __restrict__ skeys,
+                                                     const int64_t* __restrict__ seg,
+                                                     const int64_t* __restrict__ perm, int64_t n, int* err) {
+  const int nvec = int(P.dim * sizeof(OutT) / 16);
+  const int lanes = nvec < 32 ? nvec : 32;
+  const int groups_per_warp = 32 / lanes;
+  const int lane = threadIdx.x & 31;
+  const int grp = lane / lanes;
+  const int sub = lane % lanes;
+  if (grp >= groups_per_warp) return;
+  const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  const int64_t stride = n_warps * groups_per_warp;
+  for (int64_t p0 = warp_global * groups_per_warp + grp; p0 < n; p0 += stride * kGatherUnroll) {
+    const uint4* src[kGatherUnroll];
+    uint4* dst[kGatherUnroll];
+#pragma unroll
+    for (int u = 0; u < kGatherUnroll; ++u) {
+      const int64_t p = p0 + u * stride;
+      src[u] = nullptr;
+      dst[u] = nullptr;
+      if (p < n) {
+        const int64_t j = perm[p];
+        const int s = find_slot(P.slot_off, P.n_slots, j);
+        const Slot& sl = P.slots[s];
+        dst[u] = reinterpret_cast<uint4*>(static_cast<OutT*>(sl.io) + (j - P.slot_off[s]) * sl.io_stride);
+        if (skeys[p] != INT64_MAX) {
+          src[u] = reinterpret_cast<const uint4*>(stage + seg[p] * P.dim);
+        } else if (sub == 0) {
+          set_error(err, kIdOutOfRange);      // unpooled slots: only an out-of-range id has no key
+        }
+      }
+    }
+    for (int v = sub; v < nvec; v += lanes) {
+      uint4 x[kGatherUnroll];
+#pragma unroll
+      for (int u = 0; u < kGatherUnroll; ++u) x[u] = src[u] ? src[u][v] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int u = 0; u < kGatherUnroll; ++u)
+        if (dst[u]) dst[u][v] = x[u];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Pooled gather (sum / mean over a bag, pad id excluded): one warp per bag.
 // ---------------------------------------------------------------------------
 template <typename IdT, typename OutT>
@@ -474,6 +585,124 @@ __global__ void __launch_bounds__(256) reduce_update_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Same reduction with the chunk's gradient rows staged in shared memory.
+// A warp first resolves the 32 positions of its chunk lane-parallel (key,
+// perm, slot, row pointer, pooling scale), then copies all their rows into
+// its shared-memory stage with cp.async (16-byte pieces, every piece of the
+// chunk in flight at once), and reduces the runs of equal keys (found with a
+// ballot) from shared memory. Loads are no longer serialised behind the
+// previous position's perm lookup or the previous run's store.
+// ---------------------------------------------------------------------------
+constexpr int kStageMaxRowBytes = 512;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+template <typename GradT>
+__global__ void __launch_bounds__(256) reduce_update_staged_kernel(
+    const __grid_constant__ GatherParams P, OptParams O, const int64_t* __restrict__ skeys,
+    GradSrc src, int64_t total, float* __restrict__ scratch, int* __restrict__ arrivals, int* err) {
+  extern __shared__ __align__(16) unsigned char stage_smem[];
+  const unsigned FULL = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int nvec = P.dim >> 2;
+  const int rb = P.dim * int(sizeof(GradT));
+  const int v16 = rb >> 4;
+  unsigned char* wstage = stage_smem + size_t(threadIdx.x >> 5) * kChunk * rb;
+  const int64_t n_chunks = (total + kChunk - 1) / kChunk;
+  const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t c = warp_global; c < n_chunks; c += n_warps) {
+    const int64_t c0 = c * kChunk;
+    const int cn = int(min(int64_t(kChunk), total - c0));
+    int64_t myk = INT64_MAX;
+    unsigned long long gp = 0ull;
+    float gs = 0.f;
+    if (lane < cn) {
+      myk = skeys[c0 + lane];
+      if (myk != INT64_MAX) {
+        const int64_t p = src.perm[c0 + lane];
+        const int s = find_slot(P.slot_off, P.n_slots, p);
+        const Slot& sl = P.slots[s];
+        const int64_t row = src.grad_row ? src.grad_row[p] : p - P.slot_off[s];
+        gs = src.scale ? src.scale[p] : 1.f;
+        gp = reinterpret_cast<unsigned long long>(static_cast<const GradT*>(sl.io) + row * sl.io_stride);
+      }
+    }
+    const int64_t before = c0 > 0 ? skeys[c0 - 1] : INT64_MIN;
+    const int64_t after = c0 + cn < total ? skeys[c0 + cn] : INT64_MIN;
+    const int n_live = __popc(__ballot_sync(FULL, gp != 0ull));  // padding keys sort last: a prefix
+    const int pieces = n_live * v16;
+    for (int base = 0; base < pieces; base += 32) {
+      const int idx = base + lane;
+      const int row = idx / v16;
+      const unsigned long long rp = __shfl_sync(FULL, gp, row & 31);
+      if (idx < pieces) cp_async16(wstage + size_t(idx) * 16, reinterpret_cast<const unsigned char*>(rp) + (idx - row * v16) * 16);
+    }
+    cp_async_wait_all();
+    __syncwarp();
+    const int64_t up = __shfl_up_sync(FULL, myk, 1);
+    unsigned runs = __ballot_sync(FULL, lane < n_live && (lane == 0 || up != myk));
+    while (runs) {
+      const int ls = __ffs(runs) - 1;
+      runs &= runs - 1;
+      const int le = runs ? __ffs(runs) - 1 : n_live;
+      const int64_t key = __shfl_sync(FULL, myk, ls);
+      float4 acc[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int l = ls; l < le; ++l) {
+        const float sc = __shfl_sync(FULL, gs, l);
+        accum_row<GradT>(acc, reinterpret_cast<const GradT*>(wstage + size_t(l) * rb), nvec, lane, sc);
+      }
+      const bool head = ls > 0 || before != key;
+      const bool tail = le < cn || after != key;
+      if (head && tail) {
+        if (src.out_rows) store_reduced(src, c0 + ls, acc, nvec, P.dim, lane);
+        else apply_update(P, O, key, acc, nvec, lane, err);
+      } else {
+        const int64_t beg = head ? c0 + ls : lower_bound(skeys, total, key);
+        const int64_t end = tail ? c0 + le : lower_bound(skeys, total, key + 1);
+        const int64_t hc = beg / kChunk;
+        const int span = int((end - 1) / kChunk - hc + 1);
+        float* srow = scratch + hc * int64_t(P.dim);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int v = lane + 32 * k;
+          if (v < nvec) {
+            atomicAdd(srow + 4 * v + 0, acc[k].x); atomicAdd(srow + 4 * v + 1, acc[k].y);
+            atomicAdd(srow + 4 * v + 2, acc[k].z); atomicAdd(srow + 4 * v + 3, acc[k].w);
+          }
+        }
+        __threadfence();
+        __syncwarp();
+        int prev = 0;
+        if (lane == 0) prev = atomicAdd(arrivals + hc, 1);
+        prev = __shfl_sync(FULL, prev, 0);
+        if (prev == span - 1) {
+          __threadfence();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int v = lane + 32 * k;
+            if (v < nvec) {
+              acc[k] = __ldcg(reinterpret_cast<const float4*>(srow) + v);
+              reinterpret_cast<float4*>(srow)[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
+          if (lane == 0) arrivals[hc] = 0;
+          if (src.out_rows) store_reduced(src, beg, acc, nvec, P.dim, lane);
+          else apply_update(P, O, key, acc, nvec, lane, err);
+        }
+      }
+    }
+    __syncwarp();  // the stage is rewritten by the next chunk
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 
@@ -583,6 +812,55 @@ void emb_gather(std::vector<at::Tensor> ids, std::vector<at::Tensor> outs, at::T
     if (out_t == at::kBFloat16) PD_LAUNCH_GATHER(int64_t, __nv_bfloat16); else PD_LAUNCH_GATHER(int64_t, float);
   }
 #undef PD_LAUNCH_GATHER
+  PD_CHECK_LAUNCH();
+}
+
+// Deduplicated unpooled gather from a routing plan: skeys / perm are the
+// owner-sorted keys and their source positions, seg the unique index of each
+// sorted key, uniq[u] the (table key) of unique index u.
+void emb_gather_planned(std::vector<at::Tensor> ids, std::vector<at::Tensor> outs, at::Tensor slot_meta,
+                        std::vector<at::Tensor> weights, std::vector<at::Tensor> shard_ptrs,
+                        at::Tensor table_meta, int64_t dim, at::Tensor skeys, at::Tensor perm, at::Tensor seg,
+                        at::Tensor uniq, at::Tensor err) {
+  GatherParams P;
+  P.dim = int(dim);
+  TORCH_CHECK(dim % 8 == 0 && dim <= 1024, "planned gather: embedding dim must be a multiple of 8 and <= 1024");
+  std::vector<at::Tensor> e1;
+  for (size_t i = 0; i < weights.size(); ++i) e1.push_back(at::empty({0}, weights[i].options()));
+  fill_tables(P, weights, shard_ptrs, e1, e1, table_meta);
+  fill_slots(P, ids, outs, slot_meta, {}, false);
+  const int64_t total = P.slot_off[P.n_slots];
+  if (total == 0) return;
+  for (auto* t : {&skeys, &perm, &seg, &uniq})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kLong && t->is_contiguous() && t->numel() == total,
+                "planned gather: plan tensors must be int64 [n] on the device");
+  const at::ScalarType out_t = outs[0].scalar_type();
+  for (auto& o : outs) {
+    TORCH_CHECK(o.scalar_type() == out_t, "outputs of one launch must share a dtype");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(o.data_ptr()) % 16 == 0 && (o.stride(0) * o.element_size()) % 16 == 0,
+                "planned gather: output rows must be 16-byte aligned");
+  }
+  auto stage = at::empty({total, dim}, outs[0].options());   // unique rows <= positions
+  const int nvec = P.dim / 4;
+  const int rows_per_warp = nvec < 32 ? 32 / nvec : 1;
+  const int64_t blocks = grid_for((total + 8 * rows_per_warp - 1) / (8 * rows_per_warp), 1);
+  auto s = stream();
+  const int64_t* sk = skeys.data_ptr<int64_t>();
+  const int64_t* pm = perm.data_ptr<int64_t>();
+  const int64_t* sg = seg.data_ptr<int64_t>();
+  const int64_t* uq = uniq.data_ptr<int64_t>();
+  if (out_t == at::kBFloat16) {
+    auto* st = reinterpret_cast<__nv_bfloat16*>(stage.data_ptr());
+    gather_unique_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(P, uq, sg, total, st);
+    PD_CHECK_LAUNCH();
+    expand_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(P, st, sk, sg, pm, total, err.data_ptr<int>());
+  } else {
+    TORCH_CHECK(out_t == at::kFloat, "planned gather: bf16 or fp32 outputs");
+    auto* st = stage.data_ptr<float>();
+    gather_unique_kernel<float><<<blocks, 256, 0, s>>>(P, uq, sg, total, st);
+    PD_CHECK_LAUNCH();
+    expand_kernel<float><<<blocks, 256, 0, s>>>(P, st, sk, sg, pm, total, err.data_ptr<int>());
+  }
   PD_CHECK_LAUNCH();
 }
 
@@ -724,6 +1002,26 @@ void emb_reduce_update(std::vector<at::Tensor> grads, at::Tensor slot_meta,
   if (!sc.rows.defined() || sc.rows.numel() < n_chunks * dim) {
     sc.rows = at::zeros({n_chunks * dim + dim}, weights[0].options());
     sc.arrivals = at::zeros({n_chunks + 1}, weights[0].options().dtype(at::kInt));
+  }
+  // staged path: rows of at most 512 bytes, 16-byte aligned rows in every grad view
+  const int64_t rb = dim * (gt == at::kBFloat16 ? 2 : 4);
+  bool staged = rb % 16 == 0 && rb <= kStageMaxRowBytes;
+  for (auto& g : grads)
+    staged = staged && reinterpret_cast<uintptr_t>(g.data_ptr()) % 16 == 0 && (g.stride(0) * g.element_size()) % 16 == 0;
+  if (staged) {
+    const int threads = rb <= 256 ? 256 : 128;          // 64 KB of stage per block either way
+    const size_t smem = size_t(threads / 32) * kChunk * rb;
+    const int64_t blocks = grid_for((n_chunks + threads / 32 - 1) / (threads / 32), 1);
+    auto launch = [&](auto kern) {
+      PD_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+      kern<<<blocks, threads, smem, stream()>>>(P, O, sorted_keys.data_ptr<int64_t>(), src, total,
+                                                sc.rows.data_ptr<float>(), sc.arrivals.data_ptr<int>(),
+                                                err.data_ptr<int>());
+    };
+    if (gt == at::kBFloat16) launch(reduce_update_staged_kernel<__nv_bfloat16>);
+    else launch(reduce_update_staged_kernel<float>);
+    PD_CHECK_LAUNCH();
+    return;
   }
   const int64_t blocks = grid_for((n_chunks + 7) / 8, 1);
   if (gt == at::kBFloat16)

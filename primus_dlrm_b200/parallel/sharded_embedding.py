@@ -328,9 +328,10 @@ _PLAN_DIMS = 8   # distinct embedding dims one lookup may route
 class _DimPlan:
     """Backward routing of the slots of one embedding dim (see ``PeerExecutor._plan``)."""
 
-    def __init__(self, dim, sidx, tables, weights, ptrs, tmeta, meta5, skeys, perm, seg, uniq, scale, grow):
+    def __init__(self, dim, sidx, tables, weights, ptrs, tmeta, meta5, slot_ids, skeys, perm, seg, uniq, scale,
+                 grow):
         self.dim, self.sidx, self.tables, self.weights, self.ptrs = dim, sidx, tables, weights, ptrs
-        self.tmeta, self.meta5 = tmeta, meta5
+        self.tmeta, self.meta5, self.slot_ids = tmeta, meta5, slot_ids
         self.skeys, self.perm, self.seg, self.uniq = skeys, perm, seg, uniq
         self.scale, self.grow = scale, grow
 
@@ -415,72 +416,114 @@ class PeerExecutor:
     # -- lookup ------------------------------------------------------------
     def forward(self, spec: LookupSpec, ids: list[torch.Tensor], outs: list[torch.Tensor],
                 backward: bool = False) -> "_Plan | None":
-        """Gather every slot (peer loads from the owners).  With ``backward``
-        the routing of the coming backward is planned as well, on a side
-        stream that overlaps the forward: it needs the ids only."""
-        ev = self._event_pair()
-        _native_forward(spec, ids, outs)
-        self._event_end(ev)
-        return self._plan(spec, ids, outs) if backward else None
+        """Gather every slot from the owners' shards (peer loads).
 
-    def _plan(self, spec: LookupSpec, ids: list[torch.Tensor], outs: list[torch.Tensor]) -> "_Plan":
-        """Owner-sorted keys, their permutation, the unique-row segment of
-        every key and per-owner unique counts of every rank (exchanged through
-        a peer-memory board, copied to pinned host memory).  The backward then
-        runs without a host synchronisation: it waits on this plan's event,
-        which completed long before, instead of draining the compute stream."""
+        Unpooled lookups are planned first -- keys sorted by owner and row,
+        unique segments -- and gathered once per unique row in address order,
+        then expanded to every position.  With ``backward`` the plan is kept
+        for the backward and its per-owner counts are exchanged on a side
+        stream that overlaps the rest of the forward.  Pooled lookups use the
+        direct gather and plan on the side stream."""
+        ev = self._event_pair()
+        if any(sl.pool for sl in spec.slots):
+            _native_forward(spec, ids, outs)
+            self._event_end(ev)
+            if not backward:
+                return None
+            main = torch.cuda.current_stream(self.device)
+            self.side.wait_stream(main)
+            with torch.cuda.stream(self.side):
+                plan = self._plan_core(spec, ids, outs)
+            for t in ids:
+                t.record_stream(self.side)
+            for d in plan.dims:          # made on the side stream, read by the backward on this one
+                for t in (d.skeys, d.perm, d.seg, d.uniq, d.scale, d.grow):
+                    if t is not None:
+                        t.record_stream(main)
+            self._plan_counts(plan, main)
+            return plan
+        C = _ext.core()
+        plan = self._plan_core(spec, ids, outs)
+        for d in plan.dims:
+            views = [_slot_view(outs[spec.slots[i].group], spec.slots[i].col, d.dim) for i in d.sidx]
+            C.emb_gather_planned(d.slot_ids, views, d.meta5[:, :4].contiguous(), d.weights, d.ptrs, d.tmeta, d.dim,
+                                 d.skeys, d.perm, d.seg, d.uniq, spec.err)
+        self._event_end(ev)
+        if not backward:
+            return None
+        self._plan_counts(plan, torch.cuda.current_stream(self.device))
+        return plan
+
+    def _plan_core(self, spec: LookupSpec, ids: list[torch.Tensor], outs: list[torch.Tensor]) -> "_Plan":
+        """Per embedding dim, on the current stream: owner-sorted keys, their
+        permutation, the unique-row segment of every sorted key and the key of
+        every unique segment.  Needs the ids only (``outs`` give the shapes)."""
         C = _ext.core()
         W = self.world
-        main = torch.cuda.current_stream(self.device)
-        side = self.side
-        side.wait_stream(main)
         groups = list(_by_dim(spec).items())
         if len(groups) > _PLAN_DIMS:
             raise RuntimeError(f"peer exchange plans at most {_PLAN_DIMS} embedding dims, got {len(groups)}")
         plan = _Plan()
+        for dim, sidx in groups:
+            tables, remap = _launch_tables(spec, sidx)
+            weights = [t.weight for t in tables]
+            ptrs = [t.device_ptrs() for t in tables]
+            tmeta = _table_meta(tables)
+            slot_ids = [ids[i].reshape(-1) for i in sidx]
+            views, meta4, offs, any_pooled = [], [], [], False
+            for i in sidx:
+                sl = spec.slots[i]
+                views.append(_slot_view(outs[sl.group], sl.col, dim))
+                L = 0
+                if sl.pool:
+                    any_pooled = True
+                    nb = outs[sl.group].numel() // outs[sl.group].shape[-1]
+                    L = ids[i].numel() // max(nb, 1) if sl.offsets is None else 0
+                meta4.append([remap[sl.table], sl.pool, L, sl.pad_id])
+                offs.append(sl.offsets if sl.offsets is not None else ids[i].new_empty(0, dtype=torch.int64))
+            meta4 = torch.tensor(meta4, dtype=torch.int64)
+            keys = C.emb_keys(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
+            ometa = torch.tensor([[int(tmeta[k, 2]), t.chunk, _KIND_CODE.get(getattr(t, "kind", "row_wise"), 0),
+                                   t.owner if getattr(t, "owner", None) is not None else 0]
+                                  for k, t in enumerate(tables)], dtype=torch.int64)
+            skeys, perm = torch.sort(C.owner_keys(keys, ometa, W))
+            n = skeys.numel()
+            first = torch.ones(n, dtype=torch.bool, device=self.device)
+            if n > 1:
+                torch.ne(skeys[1:], skeys[:-1], out=first[1:])
+            seg = torch.cumsum(first, 0) - 1
+            uniq = torch.empty(n, dtype=torch.int64, device=self.device).scatter_(0, seg, skeys & _KEY_MASK)
+            scale = grow = None
+            if any_pooled:
+                scale, grow = C.emb_pooled_scale(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
+            meta5 = torch.cat([meta4, torch.tensor([[x.numel()] for x in slot_ids], dtype=torch.int64)], 1)
+            plan.dims.append(_DimPlan(dim, sidx, tables, weights, ptrs, tmeta, meta5, slot_ids, skeys, perm, seg,
+                                      uniq, scale, grow))
+        return plan
+
+    def _plan_counts(self, plan: "_Plan", main) -> None:
+        """Per-owner unique counts of every rank, on the side stream: counted
+        from the sorted keys (owner boundaries by binary search, no atomics),
+        written into every rank's board with peer stores, published by a
+        signal barrier and copied to pinned host memory.  The backward waits
+        on this plan's event, which completed long before, instead of
+        synchronising the host with the compute stream."""
+        C = _ext.core()
+        W = self.world
+        side = self.side
+        side.wait_stream(main)
         with torch.cuda.stream(side):
-            cnts = []
-            for dim, sidx in groups:
-                tables, remap = _launch_tables(spec, sidx)
-                weights = [t.weight for t in tables]
-                ptrs = [t.device_ptrs() for t in tables]
-                tmeta = _table_meta(tables)
-                slot_ids = [ids[i].reshape(-1) for i in sidx]
-                views, meta4, offs, any_pooled = [], [], [], False
-                for i in sidx:
-                    sl = spec.slots[i]
-                    views.append(_slot_view(outs[sl.group], sl.col, dim))
-                    L = 0
-                    if sl.pool:
-                        any_pooled = True
-                        nb = outs[sl.group].numel() // outs[sl.group].shape[-1]
-                        L = ids[i].numel() // max(nb, 1) if sl.offsets is None else 0
-                    meta4.append([remap[sl.table], sl.pool, L, sl.pad_id])
-                    offs.append(sl.offsets if sl.offsets is not None else ids[i].new_empty(0, dtype=torch.int64))
-                meta4 = torch.tensor(meta4, dtype=torch.int64)
-                keys = C.emb_keys(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
-                ometa = torch.tensor([[int(tmeta[k, 2]), t.chunk, _KIND_CODE.get(getattr(t, "kind", "row_wise"), 0),
-                                       t.owner if getattr(t, "owner", None) is not None else 0]
-                                      for k, t in enumerate(tables)], dtype=torch.int64)
-                skeys, perm = torch.sort(C.owner_keys(keys, ometa, W))
-                n = skeys.numel()
-                first = torch.ones(n, dtype=torch.bool, device=self.device)
-                if n > 1:
-                    torch.ne(skeys[1:], skeys[:-1], out=first[1:])
-                seg = torch.cumsum(first, 0) - 1
-                # owner W = replicated tables, W + 1 = padding keys (dropped)
-                own = (skeys >> _OWNER_SHIFT).clamp_(max=W + 1)
-                cnt = torch.zeros(W + 2, dtype=torch.int64, device=self.device).index_add_(0, own, first.long())
-                uniq = torch.empty(n, dtype=torch.int64, device=self.device).scatter_(0, seg, skeys & _KEY_MASK)
-                scale = grow = None
-                if any_pooled:
-                    scale, grow = C.emb_pooled_scale(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
-                meta5 = torch.cat([meta4, torch.tensor([[x.numel()] for x in slot_ids], dtype=torch.int64)], 1)
-                plan.dims.append(_DimPlan(dim, sidx, tables, weights, ptrs, tmeta, meta5, skeys, perm, seg, uniq,
-                                          scale, grow))
-                cnts.append(cnt)
             row = torch.zeros(self.plan_row, dtype=torch.int64, device=self.device)
-            row[: len(cnts) * (W + 2)] = torch.cat(cnts)
+            bounds = torch.arange(W + 2, dtype=torch.int64, device=self.device) << _OWNER_SHIFT
+            for di, d in enumerate(plan.dims):
+                n = d.skeys.numel()
+                if n == 0:
+                    continue
+                # owner W = replicated tables, W + 1 = padding keys (dropped)
+                pos = torch.searchsorted(d.skeys, bounds)
+                before = torch.where(pos > 0, d.seg[(pos - 1).clamp_(min=0)] + 1, torch.zeros_like(pos))
+                cnt = torch.diff(torch.cat([before, d.seg[-1:] + 1]))
+                row[di * (W + 2): (di + 1) * (W + 2)] = cnt
             C.peer_put_row(row, self.plan_boards, self.rank)
             self.plan_epoch += 1
             C.signal_barrier(self.plan_pads, self.rank, self.plan_epoch, self.timeout_ns, self.err)
@@ -490,12 +533,8 @@ class PeerExecutor:
             plan.event = torch.cuda.Event()
             plan.event.record(side)
         for d in plan.dims:
-            for t in (d.skeys, d.perm, d.seg, d.uniq, d.scale, d.grow):
-                if t is not None:
-                    t.record_stream(main)
-        for t in ids:
-            t.record_stream(side)
-        return plan
+            for t in (d.skeys, d.seg):
+                t.record_stream(side)
 
     def _mark(self, name: str) -> None:
         if self.time_phases:
@@ -518,7 +557,8 @@ class PeerExecutor:
         Without a plan from the forward (a lookup run outside autograd) the
         plan is made here."""
         if plan is None:
-            plan = self._plan(spec, ids, grads)
+            plan = self._plan_core(spec, ids, grads)
+            self._plan_counts(plan, torch.cuda.current_stream(self.device))
         ev = self._event_pair()
         self._mark("start")
         C = _ext.core()
