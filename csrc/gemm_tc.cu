@@ -17,7 +17,8 @@
 //               back to the MMA warp.  The MMA of tile i+1 overlaps the
 //               epilogue of tile i.
 // Fused epilogues: none | GELU (optionally also storing the pre-activation) |
-// residual add | GELU backward (acc * gelu'(pre)). An addend R (residual, or
+// GELU storing its derivative | residual add | GELU backward from the
+// pre-activation (acc * gelu'(pre)) | product with a stored derivative. An addend R (residual, or
 // a bias / positional table broadcast through zero strides) is added before
 // the activation in every mode but the GELU backward, where R is the
 // pre-activation.
@@ -42,16 +43,21 @@ constexpr int kEpiWarps = 12;  // three warps per TMEM lane quarter, splitting t
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-enum Epi : int { kNone = 0, kGelu = 1, kResidual = 2, kDGelu = 3 };
+// kGeluD: C = GELU(x), AUX = GELU'(x) for x = bf16(acc + R) -- the derivative
+// stored in the forward makes the backward's epilogue a plain product (kMul:
+// C = acc * R), with no transcendental per element.
+enum Epi : int { kNone = 0, kGelu = 1, kResidual = 2, kDGelu = 3, kGeluD = 4, kMul = 5 };
 
 struct Params {
   int M, N, K, L;
   int m_blocks, n_blocks, k_blocks, tiles;
   __nv_bfloat16* C; int64_t c_ls, c_ms;
-  const __nv_bfloat16* R; int64_t r_ls, r_ms;      // residual (kResidual) or pre-activation (kDGelu)
-  __nv_bfloat16* AUX; int64_t aux_ls, aux_ms;       // pre-activation output (kGelu), optional
+  const __nv_bfloat16* R; int64_t r_ls, r_ms;      // addend, pre-activation (kDGelu) or factor (kMul)
+  __nv_bfloat16* AUX; int64_t aux_ls, aux_ms;       // pre-activation (kGelu, optional) or GELU' (kGeluD)
   int epi;
   int a_mode, b_mode;   // TMA map dim order: 0 = {K, rows, L}, 1 = {K, L, rows}
+  int c_mode, x_mode;   // store maps of C / AUX: 0 = {N, rows, L}, 1 = {N, L, rows}
+  int r_tma, r_mode;    // R read by TMA (a full [L, M, N] view) and its map's dim order
   int b_shared;         // B has one batch shared by every l
   int* err;
 };
@@ -70,13 +76,15 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
+// try_wait with a suspend-time hint: a waiting warp sleeps until the phase
+// completes or ~0.2 ms pass instead of spinning on issue slots.
 __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
+      : "=r"(ok) : "r"(smem_u32(b)), "r"(parity), "r"(200000u) : "memory");
   return ok != 0;
 }
 // Bounded wait: false (and the error word set) after kWaitLimitNs.
@@ -105,6 +113,25 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
       ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2) : "memory");
 }
+
+// TMA store of one 32 x 32 bf16 block staged in shared memory (64-byte
+// swizzle); mode 1 maps have dims {N, L, rows}.  Rows past the tensor's end
+// are clipped by the copy engine.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+               ::"l"(map), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2) : "memory");
+}
+__device__ __forceinline__ void tma_store_rows(const CUtensorMap* map, const void* src, int mode, int n, int row,
+                                               int l) {
+  if (mode == 0) tma_store_3d(map, src, n, row, l);
+  else tma_store_3d(map, src, n, l, row);
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the staged source of every committed store has been read (the buffer may be rewritten)
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// generic-proxy shared-memory writes -> visible to the async proxy (TMA)
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // ---- tcgen05 ---------------------------------------------------------------
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -136,6 +163,27 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                ::"r"(smem_u32(bar)) : "memory");
 }
+// tcgen05.ld of 32 columns without the wait (registers undefined until
+// tc_ld_wait on the same array, which ties them to the wait instruction).
+__device__ __forceinline__ void tc_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr) : "memory");
+}
+__device__ __forceinline__ void tc_ld_wait(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :: "memory");
+}
 __device__ __forceinline__ void tc_ld32(uint32_t taddr, float* v) {
   uint32_t r[32];
   asm volatile(
@@ -161,6 +209,9 @@ __device__ __forceinline__ void tile_coords(const Params& p, int t, int& l, int&
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                            const __grid_constant__ CUtensorMap tmB,
+                                                           const __grid_constant__ CUtensorMap tmC,
+                                                           const __grid_constant__ CUtensorMap tmX,
+                                                           const __grid_constant__ CUtensorMap tmR,
                                                            const Params p) {
   constexpr uint32_t kABytes = BM * BK * 2;
   constexpr uint32_t kBBytes = BN * BK * 2;
@@ -174,12 +225,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   uint64_t* tfull = empty + STAGES;     // [2]
   uint64_t* tempty = tfull + 2;         // [2]
   uint64_t* mma_done = tempty + 2;      // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* rbar_all = mma_done + 1;    // [kEpiWarps][2]: R blocks landed (TMA)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar_all + 2 * kEpiWarps);
   // per epilogue warp: 32 x 32 bf16 staging blocks for C and R / AUX (64-byte
   // rows, 16-byte chunks XOR-swizzled by (row >> 1) & 3: conflict-free both
   // when a thread writes its own row and when 4 lanes cover one row)
+  // (the 64-byte swizzle of the TMA stores: buffers 512-byte aligned)
   uint8_t* stage_base = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(tmem_slot) + 64 + 127) & ~uintptr_t(127));  // 16-byte vector accesses
+      (reinterpret_cast<uintptr_t>(tmem_slot) + 64 + 1023) & ~uintptr_t(1023));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -187,10 +240,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], kEpiWarps * 32); }
     mbar_init(mma_done, 1);
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&rbar_all[i], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmC) : "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -268,17 +323,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   } else {
     // ---------------- epilogue ----------------
     // Warp ew owns TMEM lane quarter q (rows q*32..q*32+31 of the tile) and the
-    // 32-column chunks c with (c / 32) % 3 == part.  Per chunk: stage the
-    // residual / pre-activation block (prefetched into registers one chunk
-    // ahead), tcgen05.ld the accumulator, apply the epilogue, stage bf16 rows
-    // in swizzled smem and store them as coalesced 64-byte row segments.
+    // 32-column chunks c with (c / 32) % 3 == part.  Per chunk: the R block
+    // (residual, GELU' factor or pre-activation) arrives by TMA into a
+    // two-deep ring, issued one chunk ahead (a broadcast addend -- bias or
+    // positional table, zero strides -- is prefetched into registers
+    // instead); tcgen05.ld the accumulator, apply the epilogue, stage the
+    // bf16 block in swizzled smem and hand it to a TMA store (C, and AUX),
+    // which runs while the next chunk is computed.
     const int ew = warp - 2;
     const int q = warp & 3;
     const int part = ew >> 2;
     constexpr int kParts = kEpiWarps / 4;
-    uint8_t* stC = stage_base + ew * 2 * 2048;
-    uint8_t* stR = stC + 2048;
-    uint8_t* stX = stR;   // GELU (AUX) and residual/dGELU (R) never occur together
+    uint8_t* stC = stage_base + ew * 3 * 2048;
+    uint8_t* stR0 = stC + 2048;   // R ring: buffers stR0 and stR0 + 2048
+    uint64_t* rbar = rbar_all + 2 * ew;
+    const bool r_tma = p.r_tma != 0;
+    int kc = 0;          // chunks processed by this warp (R ring position)
+    int r_pending = 0;   // R blocks issued and not yet waited for
     const int cr = lane >> 2, cc = lane & 3;
     auto sw = [](int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); };
     const bool has_r = (p.R != nullptr);   // addend (bias / residual), or GELU's pre-activation for kDGelu
@@ -301,8 +362,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                      : make_uint4(0, 0, 0, 0);
       }
     };
+    auto issue_r = [&](int t, int c, int buf) {   // lane 0 only
+      int l, mb, nb;
+      tile_coords(p, t, l, mb, nb);
+      mbar_expect_tx(&rbar[buf], 32 * 32 * 2);
+      tma_load_rows(stR0 + (buf << 11), &tmR, &rbar[buf], p.r_mode, nb * BN + c, mb * BM + q * 32, l);
+    };
     uint4 pref[4];
-    if (has_r && first_chunk() < BN && blockIdx.x < p.tiles) load_r(blockIdx.x, first_chunk(), pref);
+    if (has_r && first_chunk() < BN && blockIdx.x < p.tiles) {
+      if (r_tma) {
+        if (lane == 0) issue_r(blockIdx.x, first_chunk(), 0);
+        r_pending = 1;
+      } else {
+        load_r(blockIdx.x, first_chunk(), pref);
+      }
+    }
     int local = 0;
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++local) {
       const int a = local & 1;
@@ -312,19 +386,36 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       tile_coords(p, t, l, mb, nb);
       const int m0 = mb * BM + q * 32;
       const int n0 = nb * BN;
-#pragma unroll 1
-      for (int c = first_chunk(); c < BN; c += kParts * 32) {
+      const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t(a * BN);
+      // one chunk: 32 accumulator columns of this warp's 32 rows, already in r
+      auto process = [&](uint32_t (&r)[32], int c) -> bool {
+        // the previous chunk's TMA stores have read the staging blocks
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        uint8_t* stR = stR0 + (r_tma ? ((kc & 1) << 11) : 0);
+        uint8_t* stX = stR;   // AUX staging reuses the R block once it has been consumed
         if (has_r) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(stR + sw(cr + 8 * i, cc)) = pref[i];
-          __syncwarp();
           int tn = t, cn = c;
           next_work(tn, cn);
-          if (tn < p.tiles) load_r(tn, cn, pref);   // in flight during this chunk
+          if (r_tma) {
+            if (tn < p.tiles) {   // the next block lands in the other buffer while this chunk runs
+              if (lane == 0) issue_r(tn, cn, (kc + 1) & 1);
+              ++r_pending;
+            }
+            const bool ok = mbar_wait(&rbar[kc & 1], uint32_t(kc >> 1) & 1u, p.err);
+            --r_pending;
+            if (!ok) { *abort_flag = 1; return false; }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(stR + sw(cr + 8 * i, cc)) = pref[i];
+            __syncwarp();
+            if (tn < p.tiles) load_r(tn, cn, pref);   // in flight during this chunk
+          }
         }
         float v[32];
-        tc_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(a * BN + c), v);
-        if (has_r && p.epi != kDGelu) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if (has_r && p.epi != kDGelu && p.epi != kMul) {
           // addend before the activation: residual, or a bias broadcast through a zero row stride
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -354,6 +445,38 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (p.epi == kGelu) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu_f(__bfloat162float(__float2bfloat16_rn(v[j])));
+        } else if (p.epi == kGeluD) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float d[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float x = __bfloat162float(__float2bfloat16_rn(v[8 * j + e]));
+              const GeluEval g = gelu_eval(x);
+              v[8 * j + e] = x * g.cdf;
+              d[e] = fmaf(x, g.pdf, g.cdf);
+            }
+            uint4 pk;
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(d[0], d[1]);
+            __nv_bfloat162 h1 = __floats2bfloat162_rn(d[2], d[3]);
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(d[4], d[5]);
+            __nv_bfloat162 h3 = __floats2bfloat162_rn(d[6], d[7]);
+            pk.x = *reinterpret_cast<uint32_t*>(&h0); pk.y = *reinterpret_cast<uint32_t*>(&h1);
+            pk.z = *reinterpret_cast<uint32_t*>(&h2); pk.w = *reinterpret_cast<uint32_t*>(&h3);
+            *reinterpret_cast<uint4*>(stX + sw(lane, j)) = pk;
+          }
+        } else if (p.epi == kMul) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 pk = *reinterpret_cast<const uint4*>(stR + sw(lane, j));
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&pk);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __bfloat1622float2(h[e]);
+              v[8 * j + 2 * e] *= f.x;
+              v[8 * j + 2 * e + 1] *= f.y;
+            }
+          }
         } else if (p.epi == kDGelu) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -378,23 +501,36 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           pk.z = *reinterpret_cast<uint32_t*>(&h2); pk.w = *reinterpret_cast<uint32_t*>(&h3);
           *reinterpret_cast<uint4*>(stC + sw(lane, j)) = pk;
         }
+        fence_async_smem();
         __syncwarp();
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = cr + 8 * i;
-          if (m0 + r < p.M) {
-            __stcs(reinterpret_cast<uint4*>(p.C + l * p.c_ls + int64_t(m0 + r) * p.c_ms + n0 + c + cc * 8),
-                   *reinterpret_cast<const uint4*>(stC + sw(r, cc)));
-            if (p.epi == kGelu && p.AUX)
-              __stcs(reinterpret_cast<uint4*>(p.AUX + l * p.aux_ls + int64_t(m0 + r) * p.aux_ms + n0 + c + cc * 8),
-                     *reinterpret_cast<const uint4*>(stX + sw(r, cc)));
-          }
+        if (lane == 0) {
+          tma_store_rows(&tmC, stC, p.c_mode, n0 + c, m0, l);
+          if ((p.epi == kGelu || p.epi == kGeluD) && p.AUX) tma_store_rows(&tmX, stX, p.x_mode, n0 + c, m0, l);
+          bulk_commit();
         }
-        __syncwarp();
+        ++kc;
+        return true;
+      };
+      constexpr int kStep = kParts * 32;
+      const int c0 = first_chunk();
+      {
+        bool ok = true;
+#pragma unroll 1
+        for (int c = c0; c < BN && ok; c += kStep) {
+          uint32_t r0[32];
+          tc_ld32_issue(tbase + c, r0);
+          tc_ld_wait(r0);
+          ok = process(r0, c);
+        }
+        if (!ok) break;
       }
       tc_fence_before();
       mbar_arrive(&tempty[a]);
     }
+    // an R block still in flight (the loop ended early) lands before the CTA exits
+    if (r_pending > 0) (void)mbar_wait(&rbar[kc & 1], uint32_t(kc >> 1) & 1u, p.err);
+    if (lane == 0) bulk_wait_all();   // every store of this warp has completed
+    __syncwarp();
   }
   // teardown: all roles are out of their loops (every wait above is bounded)
   tc_fence_before();
@@ -440,6 +576,34 @@ CUtensorMap make_map(const void* base, int64_t K, int64_t rows, int64_t L, int64
   return m;
 }
 
+// Map of a [L, rows, N] bf16 epilogue operand (C / AUX stores, R loads):
+// 32 x 32 boxes, 64-byte swizzle (the epilogue's staging layout); dim order
+// as in make_map.
+CUtensorMap make_store_map(const void* base, int64_t N, int64_t rows, int64_t L, int64_t row_stride,
+                           int64_t l_stride, int& mode) {
+  CUtensorMap m;
+  if (L <= 1) l_stride = row_stride * rows;
+  mode = (L > 1 && l_stride < row_stride) ? 1 : 0;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3];
+  if (mode == 0) {
+    dims[0] = N; dims[1] = rows; dims[2] = L;
+    strides[0] = row_stride * 2; strides[1] = l_stride * 2;
+    box[0] = 32; box[1] = 32; box[2] = 1;
+  } else {
+    dims[0] = N; dims[1] = L; dims[2] = rows;
+    strides[0] = l_stride * 2; strides[1] = row_stride * 2;
+    box[0] = 32; box[1] = 1; box[2] = 32;
+  }
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = cuTensorMapEncodeTiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (store) failed (", int(r), "): N=", N, " rows=", rows,
+              " L=", L, " row_stride=", row_stride, " l_stride=", l_stride);
+  return m;
+}
+
 // [L, rows, K] view (L may be 1): unit stride on K, 16-byte aligned rows.
 void check_operand(const at::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, ": bf16 CUDA tensor required");
@@ -450,8 +614,10 @@ void check_operand(const at::Tensor& t, const char* name) {
 }
 
 template <int BN, int STAGES>
-void launch(const CUtensorMap& ta, const CUtensorMap& tb, const tc::Params& p) {
-  constexpr size_t smem = STAGES * (tc::BM * tc::BK * 2 + BN * tc::BK * 2) + 1024 + 512 + tc::kEpiWarps * 2 * 2048;
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tcm, const CUtensorMap& txm,
+            const CUtensorMap& trm, const tc::Params& p) {
+  constexpr size_t smem = STAGES * (tc::BM * tc::BK * 2 + BN * tc::BK * 2) + 1024 + 1024 + tc::kEpiWarps * 3 * 2048;
+  static_assert(smem <= 232448, "GEMM shared memory over the 227 KB per-block limit");
   static bool attr = false;
   if (!attr) {
     PD_CHECK_CUDA(cudaFuncSetAttribute(tc::gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -459,7 +625,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const tc::Params& p) {
     attr = true;
   }
   int grid = p.tiles < num_sms() ? p.tiles : num_sms();
-  tc::gemm_kernel<BN, STAGES><<<grid, tc::kThreads, smem, stream()>>>(ta, tb, p);
+  tc::gemm_kernel<BN, STAGES><<<grid, tc::kThreads, smem, stream()>>>(ta, tb, tcm, txm, trm, p);
   PD_CHECK_LAUNCH();
 }
 
@@ -485,7 +651,10 @@ void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optiona
   p.C = reinterpret_cast<__nv_bfloat16*>(C.data_ptr()); p.c_ls = C.stride(0); p.c_ms = C.stride(1);
   p.epi = int(epi);
   p.err = err.data_ptr<int>();
-  TORCH_CHECK(!(epi == tc::kResidual || epi == tc::kDGelu) || (R && R->defined()), "this epilogue needs R");
+  TORCH_CHECK(epi >= tc::kNone && epi <= tc::kMul, "unknown epilogue ", epi);
+  TORCH_CHECK(!(epi == tc::kResidual || epi == tc::kDGelu || epi == tc::kMul) || (R && R->defined()),
+              "this epilogue needs R");
+  TORCH_CHECK(epi != tc::kGeluD || (AUX && AUX->defined()), "the GELU-derivative epilogue needs AUX");
   if (R && R->defined()) {
     // R: [L, M, N] view (stride 0 allowed on L and M: a bias or per-row-block addend)
     TORCH_CHECK(R->dim() == 3 && R->sizes() == C.sizes() && R->stride(2) == 1 && R->stride(1) % 8 == 0 &&
@@ -506,9 +675,17 @@ void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optiona
   const CUtensorMap ta = make_map(A.data_ptr(), K, M, L, A.stride(1), A.stride(0), tc::BM, p.a_mode);
   const CUtensorMap tb = make_map(B.data_ptr(), K, N, B.size(0), B.stride(1), B.stride(0), BN, p.b_mode);
   p.b_shared = (B.size(0) == 1) ? 1 : 0;
-  if (BN == 256) launch<256, 3>(ta, tb, p);
-  else if (BN == 128) launch<128, 4>(ta, tb, p);
-  else launch<64, 6>(ta, tb, p);
+  const CUtensorMap tcm = make_store_map(C.data_ptr(), N, M, L, C.stride(1), C.stride(0), p.c_mode);
+  p.x_mode = p.c_mode;
+  const CUtensorMap txm = p.AUX ? make_store_map(AUX->data_ptr(), N, M, L, AUX->stride(1), AUX->stride(0), p.x_mode)
+                                : tcm;
+  // R by TMA unless it broadcasts through a zero stride (bias / positional addend)
+  p.r_tma = (p.R && p.r_ms != 0 && (L == 1 || p.r_ls != 0)) ? 1 : 0;
+  p.r_mode = 0;
+  const CUtensorMap trm = p.r_tma ? make_store_map(R->data_ptr(), N, M, L, R->stride(1), R->stride(0), p.r_mode) : tcm;
+  if (BN == 256) launch<256, 3>(ta, tb, tcm, txm, trm, p);
+  else if (BN == 128) launch<128, 4>(ta, tb, tcm, txm, trm, p);
+  else launch<64, 6>(ta, tb, tcm, txm, trm, p);
 }
 
 }  // namespace pd

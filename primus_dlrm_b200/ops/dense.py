@@ -33,7 +33,9 @@ def _cast_w(w: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
     return w.to(like.dtype) if w.dtype != like.dtype else w
 
 
-_EPI = {"": 0, None: 0, "gelu": 1, "residual": 2, "dgelu": 3}
+# gelu_d: GELU with its derivative stored in AUX; mul: acc * R (the backward
+# through that stored derivative)
+_EPI = {"": 0, None: 0, "gelu": 1, "residual": 2, "dgelu": 3, "gelu_d": 4, "mul": 5}
 _err_words: dict = {}
 
 
@@ -102,18 +104,18 @@ class _MixedLinearNative(torch.autograd.Function):
         B, T, _ = xb.shape
         N = ws.shape[0]
         y = torch.empty(B, T, N, dtype=torch.bfloat16, device=x.device)
-        pre = torch.empty_like(y) if act == "gelu" else None
-        _mixed_tc(xb, n_s, ws, wn, y, "gelu" if act == "gelu" else None, AUX=pre)
-        ctx.save_for_backward(xb, ws, wn, pre if pre is not None else y.new_empty(0))
+        dact = torch.empty_like(y) if act == "gelu" else None       # GELU'(pre-activation)
+        _mixed_tc(xb, n_s, ws, wn, y, "gelu_d" if act == "gelu" else None, AUX=dact)
+        ctx.save_for_backward(xb, ws, wn, dact if dact is not None else y.new_empty(0))
         ctx.n_s, ctx.act, ctx.wdt = n_s, act, (w_s.dtype, w_ns.dtype)
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        xb, ws, wn, pre = ctx.saved_tensors
+        xb, ws, wn, dact = ctx.saved_tensors
         dy = dy.contiguous().to(torch.bfloat16)
         if ctx.act == "gelu":
-            dy = torch.ops.aten.gelu_backward(dy, pre)
+            dy = dy * dact
         B, T, K = xb.shape
         dx = torch.empty(B, T, K, dtype=torch.bfloat16, device=xb.device)
         _mixed_tc(dy, ctx.n_s, ws.t().contiguous(), wn.transpose(1, 2).contiguous(), dx)
@@ -123,9 +125,9 @@ class _MixedLinearNative(torch.autograd.Function):
 
 class MixedFFNNative(torch.autograd.Function):
     """out = z + W2(GELU(W1 x)) for the mixed S / NS parameterisation, on the
-    tcgen05 GEMM: GELU (+ pre-activation store) fused into the up projection,
-    the residual add into the down projection, and GELU's backward into the
-    down projection's data-gradient GEMM."""
+    tcgen05 GEMM: GELU fused into the up projection (which also stores GELU'
+    of the pre-activation), the residual add into the down projection, and the
+    product with GELU' into the down projection's data-gradient GEMM."""
 
     @staticmethod
     def forward(ctx, x, z, w1, w2, wn1, wn2, n_s: int):
@@ -134,24 +136,24 @@ class MixedFFNNative(torch.autograd.Function):
         B, T, D = xb.shape
         F_ = bw[0].shape[0]
         h = torch.empty(B, T, F_, dtype=torch.bfloat16, device=x.device)
-        pre = torch.empty_like(h)
-        _mixed_tc(xb, n_s, bw[0], bw[2], h, "gelu", AUX=pre)
+        dact = torch.empty_like(h)                                # GELU'(pre-activation)
+        _mixed_tc(xb, n_s, bw[0], bw[2], h, "gelu_d", AUX=dact)
         out = torch.empty(B, T, D, dtype=torch.bfloat16, device=x.device)
         _mixed_tc(h, n_s, bw[1], bw[3], out, "residual", R=z)
-        ctx.save_for_backward(xb, h, pre, *bw)
+        ctx.save_for_backward(xb, h, dact, *bw)
         ctx.n_s = n_s
         ctx.wdt = [w.dtype for w in (w1, w2, wn1, wn2)]
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        xb, h, pre, w1, w2, wn1, wn2 = ctx.saved_tensors
+        xb, h, dact, w1, w2, wn1, wn2 = ctx.saved_tensors
         n_s = ctx.n_s
         dout = dout.contiguous().to(torch.bfloat16)
         B, T, D = xb.shape
         F_ = w1.shape[0]
         dpre = torch.empty(B, T, F_, dtype=torch.bfloat16, device=xb.device)
-        _mixed_tc(dout, n_s, w2.t().contiguous(), wn2.transpose(1, 2).contiguous(), dpre, "dgelu", R=pre)
+        _mixed_tc(dout, n_s, w2.t().contiguous(), wn2.transpose(1, 2).contiguous(), dpre, "mul", R=dact)
         dw2, dwn2 = _dw(dout, h, n_s, (ctx.wdt[1], ctx.wdt[3]))
         dx = torch.empty(B, T, D, dtype=torch.bfloat16, device=xb.device)
         _mixed_tc(dpre, n_s, w1.t().contiguous(), wn1.transpose(1, 2).contiguous(), dx)
@@ -229,10 +231,10 @@ def mixed_linear(x: torch.Tensor, n_s: int, w_s: torch.Tensor, w_ns: torch.Tenso
 
 class _MLP2Native(torch.autograd.Function):
     """y = W2 GELU(W1 x + b1) + b2 (+ addend[l]) on the tcgen05 GEMM: the bias
-    and GELU (with the pre-activation stored for backward) fused into the
-    first GEMM's epilogue, bias + per-position addend (the tokenizer's
-    positional embedding) into the second's, GELU' into the data-gradient
-    GEMM. x [B, L, K]; addend [L, N] or None."""
+    and GELU (with GELU' of the pre-activation stored for backward) fused into
+    the first GEMM's epilogue, bias + per-position addend (the tokenizer's
+    positional embedding) into the second's, the product with GELU' into the
+    data-gradient GEMM. x [B, L, K]; addend [L, N] or None."""
 
     @staticmethod
     def forward(ctx, x, w1, b1, w2, b2, addend):
@@ -244,8 +246,8 @@ class _MLP2Native(torch.autograd.Function):
         v = lambda t: t.reshape(1, rows, t.shape[-1])  # noqa: E731
         r1 = b1.to(torch.bfloat16).reshape(1, 1, F_).expand(1, rows, F_)
         h = torch.empty(B, L, F_, dtype=torch.bfloat16, device=x.device)
-        pre = torch.empty_like(h)
-        tc_gemm(v(xb), w1b.reshape(1, F_, K), v(h), "gelu", R=r1, AUX=v(pre))
+        dact = torch.empty_like(h)                                # GELU'(pre-activation)
+        tc_gemm(v(xb), w1b.reshape(1, F_, K), v(h), "gelu_d", R=r1, AUX=v(dact))
         add2 = b2.to(torch.bfloat16).reshape(1, N)
         if addend is not None:
             add2 = (addend.to(torch.float32) + b2.to(torch.float32)).to(torch.bfloat16)
@@ -254,14 +256,14 @@ class _MLP2Native(torch.autograd.Function):
             r2 = add2.reshape(1, 1, N).expand(B, L, N)
         out = torch.empty(B, L, N, dtype=torch.bfloat16, device=x.device)
         tc_gemm(v(h), w2b.reshape(1, N, F_), v(out), None, R=v(r2))
-        ctx.save_for_backward(xb, h, pre, w1b, w2b)
+        ctx.save_for_backward(xb, h, dact, w1b, w2b)
         ctx.meta = (w1.dtype, b1.dtype, w2.dtype, b2.dtype, addend is not None,
                     addend.dtype if addend is not None else None)
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        xb, h, pre, w1b, w2b = ctx.saved_tensors
+        xb, h, dact, w1b, w2b = ctx.saved_tensors
         dt_w1, dt_b1, dt_w2, dt_b2, has_add, dt_add = ctx.meta
         dout = dout.contiguous().to(torch.bfloat16)
         B, L, N = dout.shape
@@ -269,7 +271,7 @@ class _MLP2Native(torch.autograd.Function):
         rows = B * L
         v = lambda t: t.reshape(1, rows, t.shape[-1])  # noqa: E731
         dpre = torch.empty(B, L, F_, dtype=torch.bfloat16, device=dout.device)
-        tc_gemm(v(dout), w2b.t().contiguous().reshape(1, F_, N), v(dpre), "dgelu", R=v(pre))
+        tc_gemm(v(dout), w2b.t().contiguous().reshape(1, F_, N), v(dpre), "mul", R=v(dact))
         dx = torch.empty(B, L, K, dtype=torch.bfloat16, device=dout.device)
         tc_gemm(v(dpre), w1b.t().contiguous().reshape(1, K, F_), v(dx))
         d2 = dout.reshape(rows, N)

@@ -56,6 +56,32 @@ def test_epilogues():
     torch.testing.assert_close(c.float(), acc * x.grad, rtol=3e-2, atol=0.5)
 
 
+def test_gelu_derivative_store_and_product_epilogues():
+    """gelu_d: C = GELU(x), AUX = GELU'(x) for x = bf16(acc); mul: C = acc * R.
+    Against fp32 autograd of torch's exact-erf GELU."""
+    from primus_dlrm_b200.ops.dense import tc_gemm
+    M, N, K = 700, 256, 128
+    a, b = _bf(1, M, K), _bf(1, N, K)
+    acc = a.float() @ b.float().transpose(1, 2)
+    c = torch.empty(1, M, N, device="cuda", dtype=torch.bfloat16)
+    d = torch.empty_like(c)
+    tc_gemm(a, b, c, "gelu_d", AUX=d)
+    x = acc.to(torch.bfloat16).float().requires_grad_(True)
+    y = F.gelu(x)
+    y.backward(torch.ones_like(y))
+    torch.testing.assert_close(c.float(), y.detach(), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(d.float(), x.grad, rtol=2e-2, atol=2e-2)
+    # with an addend (bias broadcast through zero strides) before the activation
+    bias = (torch.randn(N, device="cuda") * 0.5).to(torch.bfloat16)
+    tc_gemm(a, b, c, "gelu_d", R=bias.view(1, 1, N).expand(1, M, N), AUX=d)
+    x2 = (acc + bias.float()).to(torch.bfloat16).float().requires_grad_(True)
+    F.gelu(x2).backward(torch.ones_like(x2))
+    torch.testing.assert_close(d.float(), x2.grad, rtol=2e-2, atol=2e-2)
+    r = _bf(1, M, N)
+    tc_gemm(a, b, c, "mul", R=r)
+    torch.testing.assert_close(c.float(), acc * r.float(), rtol=2e-2, atol=0.5)
+
+
 def test_mixed_linear_and_ffn_match_torch_path():
     import os
 
