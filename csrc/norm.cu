@@ -29,6 +29,7 @@ __device__ __forceinline__ Vec8 pack8(const float* f) {
   for (int k = 0; k < 4; ++k) v.h[k] = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
   return v;
 }
+__device__ __forceinline__ Vec8 as_vec8(uint4 u) { return *reinterpret_cast<const Vec8*>(&u); }
 __device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 // Rows per warp per loop iteration: the loads of all RPW rows are issued
@@ -39,8 +40,8 @@ __device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2
 // partials) live in registers when a lane owns at most 16 columns; wider rows
 // read the weight through L1 and accumulate the partials in shared memory.
 template <int NV> struct NormRows { static constexpr int value = NV == 1 ? 4 : (NV == 2 ? 2 : 1); };
-// The backward holds three row vectors (x, dy, dz) per row: half the rows.
-template <int NV> struct NormRowsBwd { static constexpr int value = NV == 1 ? 2 : 1; };
+// The backward keeps only the extra-gradient vector of a row in registers.
+template <int NV> struct NormRowsBwd { static constexpr int value = NV == 1 ? 4 : (NV == 2 ? 2 : 1); };
 
 // Batch/row split of a flat row index; 32-bit division whenever it fits.
 __device__ __forceinline__ void split_row(int64_t r, int64_t rpb, bool small, int64_t& bb, int64_t& ii) {
@@ -210,6 +211,10 @@ __global__ void __launch_bounds__(256) norm_fwd_kernel(
 // that a pre-norm block carries on as its residual -- so the slice's gradient
 // is added here instead of through a zero-filled full-size copy.  Writes dx
 // (bf16) and accumulates dw/db.
+//
+// Pass 1 reads x and dy of RPW rows (all loads issued first, through L1) for
+// the two row sums; pass 2 reads them again -- L1 hits -- so only the
+// extra-gradient vectors stay in registers across the reductions.
 template <int KIND, int NV>
 __global__ void __launch_bounds__(256, 2) norm_bwd_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ dy,
@@ -235,63 +240,65 @@ __global__ void __launch_bounds__(256, 2) norm_bwd_kernel(
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nw = (int64_t(gridDim.x) * blockDim.x) >> 5;
   for (int64_t r0 = warp * RPW; r0 < rows; r0 += nw * RPW) {
-    Vec8 xv[RPW][NV], dv[RPW][NV], ev[RPW][NV];
-    float rstd[RPW], mean[RPW];
+    Vec8 ev[RPW][NV];
+    float rstd[RPW], mean[RPW], s1[RPW], s2[RPW];
     bool has_ex[RPW];
+    // pass 1: issue every load of the group, then the row sums and the column partials
+    {
+      Vec8 xv[RPW][NV], dv[RPW][NV];
 #pragma unroll
-    for (int j = 0; j < RPW; ++j) {
-      const int64_t r = r0 + j;
-      rstd[j] = 0.f;
-      mean[j] = 0.f;
-      has_ex[j] = false;
-      if (r < rows) {
-        rstd[j] = stat_rstd[r];
-        if (KIND == 1) mean[j] = stat_mean[r];
-        const Vec8* er = nullptr;
-        if (dz_extra) {
-          int64_t bb, ii;
-          split_row(r, ex_rpb, small, bb, ii);
-          if (ii >= ex_off) er = reinterpret_cast<const Vec8*>(dz_extra + (bb * (ex_rpb - ex_off) + ii - ex_off) * D);
+      for (int j = 0; j < RPW; ++j) {
+        const int64_t r = r0 + j;
+        rstd[j] = 0.f;
+        mean[j] = 0.f;
+        has_ex[j] = false;
+        if (r < rows) {
+          rstd[j] = __ldg(stat_rstd + r);
+          if (KIND == 1) mean[j] = __ldg(stat_mean + r);
+          const Vec8* er = nullptr;
+          if (dz_extra) {
+            int64_t bb, ii;
+            split_row(r, ex_rpb, small, bb, ii);
+            if (ii >= ex_off) er = reinterpret_cast<const Vec8*>(dz_extra + (bb * (ex_rpb - ex_off) + ii - ex_off) * D);
+          }
+          has_ex[j] = er != nullptr;
+#pragma unroll
+          for (int k = 0; k < NV; ++k) {
+            const int c = lane + 32 * k;
+            if (c < nvec) {
+              xv[j][k] = as_vec8(__ldg(reinterpret_cast<const uint4*>(x + r * D) + c));
+              dv[j][k] = as_vec8(__ldg(reinterpret_cast<const uint4*>(dy + r * D) + c));
+              if (er) ev[j][k] = as_vec8(__ldcs(reinterpret_cast<const uint4*>(er) + c));
+            }
+          }
         }
-        has_ex[j] = er != nullptr;
+      }
+#pragma unroll
+      for (int j = 0; j < RPW; ++j) {
+        s1[j] = 0.f;
+        s2[j] = 0.f;
+        if (r0 + j >= rows) continue;
 #pragma unroll
         for (int k = 0; k < NV; ++k) {
           const int c = lane + 32 * k;
           if (c < nvec) {
-            xv[j][k] = reinterpret_cast<const Vec8*>(x + r * D)[c];
-            dv[j][k] = reinterpret_cast<const Vec8*>(dy + r * D)[c];
-            if (er) ev[j][k] = er[c];
-          }
-        }
-      }
-    }
-    // pass 1: row sums of g * xhat and g (g = dy * w), column partials of dW / dB
-    float s1[RPW], s2[RPW];
+            float xf[8], df[8], wk[8];
+            unpack8(xv[j][k], xf);
+            unpack8(dv[j][k], df);
+            wc.get(w, k, c, wk);
 #pragma unroll
-    for (int j = 0; j < RPW; ++j) {
-      s1[j] = 0.f;
-      s2[j] = 0.f;
-      if (r0 + j >= rows) continue;
-#pragma unroll
-      for (int k = 0; k < NV; ++k) {
-        const int c = lane + 32 * k;
-        if (c < nvec) {
-          float xf[8], df[8], wk[8];
-          unpack8(xv[j][k], xf);
-          unpack8(dv[j][k], df);
-          wc.get(w, k, c, wk);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float xh = (xf[e] - mean[j]) * rstd[j];
-            const float g = df[e] * wk[e];
-            s1[j] += g * xh;
-            s2[j] += g;
-            if (HOLD) {
-              pw[HOLD ? k : 0][e] += df[e] * xh;
-              pb[HOLD ? k : 0][e] += df[e];
-            } else {
-              atomicAdd(&sm[8 * c + e], df[e] * xh);
-              if (KIND == 1) atomicAdd(&sm[D + 8 * c + e], df[e]);
+            for (int e = 0; e < 8; ++e) {
+              const float xh = (xf[e] - mean[j]) * rstd[j];
+              const float g = df[e] * wk[e];
+              s1[j] += g * xh;
+              s2[j] += g;
+              if (HOLD) {
+                pw[HOLD ? k : 0][e] += df[e] * xh;
+                pb[HOLD ? k : 0][e] += df[e];
+              } else {
+                atomicAdd(&sm[8 * c + e], df[e] * xh);
+                if (KIND == 1) atomicAdd(&sm[D + 8 * c + e], df[e]);
+              }
             }
           }
         }
@@ -299,6 +306,7 @@ __global__ void __launch_bounds__(256, 2) norm_bwd_kernel(
     }
     warp_sum_n(s1);
     warp_sum_n(s2);
+    // pass 2: x and dy again (L1), dx out
 #pragma unroll
     for (int j = 0; j < RPW; ++j) {
       const int64_t r = r0 + j;
@@ -309,8 +317,10 @@ __global__ void __launch_bounds__(256, 2) norm_bwd_kernel(
         const int c = lane + 32 * k;
         if (c < nvec) {
           float xf[8], df[8], wk[8], ex[8], o[8];
-          unpack8(xv[j][k], xf);
-          unpack8(dv[j][k], df);
+          const uint4 xr = __ldg(reinterpret_cast<const uint4*>(x + r * D) + c);
+          const uint4 dr = __ldg(reinterpret_cast<const uint4*>(dy + r * D) + c);
+          unpack8(as_vec8(xr), xf);
+          unpack8(as_vec8(dr), df);
           wc.get(w, k, c, wk);
           if (has_ex[j]) unpack8(ev[j][k], ex);
 #pragma unroll
@@ -448,7 +458,7 @@ std::vector<at::Tensor> norm_bwd(at::Tensor xin, at::Tensor dy, c10::optional<at
   auto dw = at::zeros({D}, w.options());
   at::Tensor db = kind == 1 ? at::zeros({D}, w.options()) : at::Tensor();
   if (rows == 0) return {dx, dw, db};
-  const int64_t want = (rows + 16 - 1) / 16;   // 8 warps x 2 rows at D <= 256
+  const int64_t want = (rows + 32 - 1) / 32;   // 8 warps x 4 rows at D <= 256
   const size_t smem = 2 * D * sizeof(float);
   auto xp = reinterpret_cast<const __nv_bfloat16*>(xin.data_ptr());
   auto dyp = reinterpret_cast<const __nv_bfloat16*>(dyc.data_ptr());
