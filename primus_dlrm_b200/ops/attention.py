@@ -68,11 +68,18 @@ def _tc_fwd_ok(qkv: torch.Tensor) -> bool:
             and os.environ.get("PD_ATTN_TC_FWD", "0") == "1")
 
 
+# Below this many queries the mma.sync backward is faster on B200 (v6 pyramid,
+# batch 2048: q 283 / kv 409 3.54 vs 3.66 ms, q 158 / kv 283 1.85 vs 2.21 ms,
+# q 32 / kv 158 0.56 vs 1.09 ms; from q 409 up the tcgen05 kernel wins).
+_TC_BWD_MIN_Q = int(os.environ.get("PD_ATTN_TC_BWD_MIN_Q", "300"))
+
+
 def _tc_bwd_ok(qkv: torch.Tensor, q_len: int) -> bool:
-    """tcgen05 backward: contiguous qkv, d = 32, q_len within its shared-memory dQ block."""
+    """tcgen05 backward: contiguous qkv, d = 32, q_len within its shared-memory
+    dQ block and above the size where it beats the mma.sync backward."""
     g = _ext.gemm()
     return (hasattr(g, "fmha_bwd_tc") and qkv.is_contiguous() and qkv.shape[-1] == 32
-            and q_len <= g.fmha_bwd_tc_max_q() and os.environ.get("PD_ATTN_TC_BWD", "1") != "0")
+            and _TC_BWD_MIN_Q <= q_len <= g.fmha_bwd_tc_max_q() and os.environ.get("PD_ATTN_TC_BWD", "1") != "0")
 
 
 def _err_word(device) -> torch.Tensor:
