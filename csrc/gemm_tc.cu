@@ -59,6 +59,7 @@ struct Params {
   int c_mode, x_mode;   // store maps of C / AUX: 0 = {N, rows, L}, 1 = {N, L, rows}
   int r_tma, r_mode;    // R read by TMA (a full [L, M, N] view) and its map's dim order
   int b_shared;         // B has one batch shared by every l
+  int b_kn;             // B stored [L, K, N] (N contiguous: a weight used transposed), loaded MN-major
   int* err;
 };
 
@@ -146,6 +147,18 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   d |= uint64_t(1024 >> 4) << 32;               // stride byte offset: 8 rows x 128 B
   d |= uint64_t(1) << 46;                       // descriptor version (sm_100)
   d |= uint64_t(2) << 61;                       // SWIZZLE_128B
+  return d;
+}
+// MN-major, 128-byte-swizzled B tile: BN / 64 groups of [64 k-rows][64 n]
+// (8 KB each, 128 B per k-row); a 16-row k-step starts 2048 B further, the
+// groups are 8192 B apart (leading byte offset), 8-row atoms 1024 B apart.
+__device__ __forceinline__ uint64_t smem_desc_mn(uint32_t addr) {
+  uint64_t d = 0;
+  d |= uint64_t((addr >> 4) & 0x3FFF);
+  d |= uint64_t(8192 >> 4) << 16;
+  d |= uint64_t(1024 >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(2) << 61;
   return d;
 }
 // kind::f16 instruction descriptor: f32 accumulate, bf16 A/B, both K-major.
@@ -273,7 +286,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           if (!mbar_wait(&empty[stage], phase, p.err)) { *abort_flag = 1; break; }
           mbar_expect_tx(&full[stage], kABytes + kBBytes);
           tma_load_rows(sA + stage * kABytes, &tmA, &full[stage], p.a_mode, kb * BK, mb * BM, l);
-          tma_load_rows(sB + stage * kBBytes, &tmB, &full[stage], p.b_mode, kb * BK, nb * BN, p.b_shared ? 0 : l);
+          if (p.b_kn) {
+#pragma unroll
+            for (int g = 0; g < BN / 64; ++g)   // [64 k-rows][64 n] boxes
+              tma_load_rows(sB + stage * kBBytes + g * 8192, &tmB, &full[stage], p.b_mode, nb * BN + 64 * g, kb * BK,
+                            p.b_shared ? 0 : l);
+          } else {
+            tma_load_rows(sB + stage * kBBytes, &tmB, &full[stage], p.b_mode, kb * BK, nb * BN, p.b_shared ? 0 : l);
+          }
           ++issued_on[stage];
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -291,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc = instr_desc(BM, BN);
+      const uint32_t idesc_run = idesc | (p.b_kn ? (1u << 16) : 0u);   // B MN-major
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -308,7 +329,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           const uint32_t b_addr = smem_u32(sB + stage * kBBytes);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            tc_mma(d, smem_desc(a_addr + k * 32), smem_desc(b_addr + k * 32), idesc, (kb | k) ? 1u : 0u);
+            const uint64_t db = p.b_kn ? smem_desc_mn(b_addr + k * 2048) : smem_desc(b_addr + k * 32);
+            tc_mma(d, smem_desc(a_addr + k * 32), db, idesc_run, (kb | k) ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -631,15 +653,17 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tcm
 
 }  // namespace
 
-// C[l, m, :N] = epi(A[l] @ B[l]^T).  A: [L, M, K], B: [L or 1, N, K], C/R/AUX: [L, M, N] views
+// C[l, m, :N] = epi(A[l] @ B[l]^T).  A: [L, M, K], B: [L or 1, N, K] -- or, with b_kn,
+// [L or 1, K, N] (a weight used transposed, read MN-major) -- C/R/AUX: [L, M, N] views
 // (unit column stride).  epi: 0 none, 1 gelu (aux = pre-activation, optional), 2 residual (R),
-// 3 dgelu (R = pre-activation).
+// 3 dgelu (R = pre-activation), 4 gelu storing gelu' in AUX, 5 product with R.
 void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optional<at::Tensor> R,
-             c10::optional<at::Tensor> AUX, at::Tensor err) {
+             c10::optional<at::Tensor> AUX, at::Tensor err, bool b_kn) {
   check_operand(A, "A");
   check_operand(B, "B");
-  const int64_t L = A.size(0), M = A.size(1), K = A.size(2), N = B.size(1);
-  TORCH_CHECK(B.size(2) == K && (B.size(0) == L || B.size(0) == 1), "B must be [L or 1, N, K]");
+  const int64_t L = A.size(0), M = A.size(1), K = A.size(2), N = b_kn ? B.size(2) : B.size(1);
+  TORCH_CHECK((b_kn ? B.size(1) : B.size(2)) == K && (B.size(0) == L || B.size(0) == 1),
+              b_kn ? "B must be [L or 1, K, N]" : "B must be [L or 1, N, K]");
   TORCH_CHECK(N % 64 == 0, "N must be a multiple of 64");
   TORCH_CHECK(C.dim() == 3 && C.size(0) == L && C.size(1) == M && C.size(2) == N && C.stride(2) == 1 &&
               C.scalar_type() == at::kBFloat16 && C.stride(1) % 8 == 0 && (C.size(0) == 1 || C.stride(0) % 8 == 0) &&
@@ -673,7 +697,10 @@ void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optiona
   p.n_blocks = int(N / BN);
   p.tiles = int(L) * p.m_blocks * p.n_blocks;
   const CUtensorMap ta = make_map(A.data_ptr(), K, M, L, A.stride(1), A.stride(0), tc::BM, p.a_mode);
-  const CUtensorMap tb = make_map(B.data_ptr(), K, N, B.size(0), B.stride(1), B.stride(0), BN, p.b_mode);
+  p.b_kn = b_kn ? 1 : 0;
+  // MN-major B: boxes of 64 n x 64 k-rows over dims {N, K, L}
+  const CUtensorMap tb = b_kn ? make_map(B.data_ptr(), N, K, B.size(0), B.stride(1), B.stride(0), tc::BK, p.b_mode)
+                              : make_map(B.data_ptr(), K, N, B.size(0), B.stride(1), B.stride(0), BN, p.b_mode);
   p.b_shared = (B.size(0) == 1) ? 1 : 0;
   const CUtensorMap tcm = make_store_map(C.data_ptr(), N, M, L, C.stride(1), C.stride(0), p.c_mode);
   p.x_mode = p.c_mode;

@@ -54,10 +54,12 @@ def gemm_error_code(device) -> int:
 
 
 def tc_gemm(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, epi: str | None = None,
-            R: torch.Tensor | None = None, AUX: torch.Tensor | None = None) -> torch.Tensor:
+            R: torch.Tensor | None = None, AUX: torch.Tensor | None = None, b_kn: bool = False) -> torch.Tensor:
     """C[l] = epi(A[l] @ B[l]^T) on the sm_100a tcgen05 kernel; A [L, M, K],
-    B [L or 1, N, K], C/R/AUX [L, M, N] (bf16 views, unit stride on the last dim)."""
-    _ext.gemm().tc_gemm(A, B, C, _EPI[epi], R, AUX, _err(A.device))
+    B [L or 1, N, K] -- or with ``b_kn`` [L or 1, K, N], a weight used
+    transposed, read in place -- C/R/AUX [L, M, N] (bf16 views, unit stride on
+    the last dim)."""
+    _ext.gemm().tc_gemm(A, B, C, _EPI[epi], R, AUX, _err(A.device), b_kn)
     return C
 
 
@@ -65,16 +67,18 @@ def _tc_ok(x: torch.Tensor, K: int, N: int) -> bool:
     return x.dtype == torch.bfloat16 and K % 8 == 0 and N % 64 == 0 and x.data_ptr() % 16 == 0
 
 
-def _mixed_tc(x, n_s, ws, wn, out, epi=None, R=None, AUX=None):
+def _mixed_tc(x, n_s, ws, wn, out, epi=None, R=None, AUX=None, b_kn=False):
     """out = epi(mixed(x)) with the tcgen05 GEMM: all T rows with ws, then the
-    NS rows (one batch per token) with wn.  x [B, T, K]; ws [N, K]; wn [NS, N, K]."""
+    NS rows (one batch per token) with wn.  x [B, T, K]; ws [N, K]; wn [NS, N, K]
+    -- or with ``b_kn`` the forward weights ws [K, N], wn [NS, K, N] applied
+    transposed (the data gradient), read in place."""
     Bsz, T, K = x.shape
-    N = ws.shape[0]
+    N = ws.shape[1] if b_kn else ws.shape[0]
     v = lambda t: t.reshape(1, Bsz * T, t.shape[-1]) if t is not None else None
-    tc_gemm(v(x), ws.reshape(1, N, K), v(out), epi, v(R), v(AUX))
+    tc_gemm(v(x), ws.reshape(1, *ws.shape), v(out), epi, v(R), v(AUX), b_kn=b_kn)
     if T > n_s:
         tr = lambda t: t[:, n_s:].transpose(0, 1) if t is not None else None
-        tc_gemm(tr(x), wn, tr(out), epi, tr(R), tr(AUX))
+        tc_gemm(tr(x), wn, tr(out), epi, tr(R), tr(AUX), b_kn=b_kn)
     return out
 
 
@@ -118,7 +122,7 @@ class _MixedLinearNative(torch.autograd.Function):
             dy = dy * dact
         B, T, K = xb.shape
         dx = torch.empty(B, T, K, dtype=torch.bfloat16, device=xb.device)
-        _mixed_tc(dy, ctx.n_s, ws.t().contiguous(), wn.transpose(1, 2).contiguous(), dx)
+        _mixed_tc(dy, ctx.n_s, ws, wn, dx, b_kn=True)
         dws, dwn = _dw(dy, xb, ctx.n_s, ctx.wdt)
         return dx, dws, dwn, None, None
 
@@ -153,10 +157,10 @@ class MixedFFNNative(torch.autograd.Function):
         B, T, D = xb.shape
         F_ = w1.shape[0]
         dpre = torch.empty(B, T, F_, dtype=torch.bfloat16, device=xb.device)
-        _mixed_tc(dout, n_s, w2.t().contiguous(), wn2.transpose(1, 2).contiguous(), dpre, "mul", R=dact)
+        _mixed_tc(dout, n_s, w2, wn2, dpre, "mul", R=dact, b_kn=True)
         dw2, dwn2 = _dw(dout, h, n_s, (ctx.wdt[1], ctx.wdt[3]))
         dx = torch.empty(B, T, D, dtype=torch.bfloat16, device=xb.device)
-        _mixed_tc(dpre, n_s, w1.t().contiguous(), wn1.transpose(1, 2).contiguous(), dx)
+        _mixed_tc(dpre, n_s, w1, wn1, dx, b_kn=True)
         dw1, dwn1 = _dw(dpre, xb, n_s, (ctx.wdt[0], ctx.wdt[2]))
         return dx, dout, dw1, dw2, dwn1, dwn2, None
 
@@ -271,9 +275,9 @@ class _MLP2Native(torch.autograd.Function):
         rows = B * L
         v = lambda t: t.reshape(1, rows, t.shape[-1])  # noqa: E731
         dpre = torch.empty(B, L, F_, dtype=torch.bfloat16, device=dout.device)
-        tc_gemm(v(dout), w2b.t().contiguous().reshape(1, F_, N), v(dpre), "mul", R=v(dact))
+        tc_gemm(v(dout), w2b.reshape(1, N, F_), v(dpre), "mul", R=v(dact), b_kn=True)
         dx = torch.empty(B, L, K, dtype=torch.bfloat16, device=dout.device)
-        tc_gemm(v(dpre), w1b.t().contiguous().reshape(1, K, F_), v(dx))
+        tc_gemm(v(dpre), w1b.reshape(1, F_, K), v(dx), b_kn=True)
         d2 = dout.reshape(rows, N)
         dp = dpre.reshape(rows, F_)
         dw2 = torch.matmul(d2.t(), h.reshape(rows, F_)).to(dt_w2)

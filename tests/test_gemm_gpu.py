@@ -23,6 +23,31 @@ def test_plain(M, N, K):
     assert gemm_error_code("cuda") == 0
 
 
+@pytest.mark.parametrize("M,N,K", [(1000, 256, 768), (129, 1024, 256), (300, 256, 1024), (77, 64, 200)])
+def test_b_transposed_in_place(M, N, K):
+    """B given as a stored weight [K, N] (N contiguous), read MN-major: C = A @ W."""
+    from primus_dlrm_b200.ops.dense import tc_gemm, gemm_error_code
+    a, w = _bf(1, M, K), _bf(1, K, N)
+    c = torch.empty(1, M, N, device="cuda", dtype=torch.bfloat16)
+    tc_gemm(a, w, c, b_kn=True)
+    ref = a.float() @ w.float()
+    torch.testing.assert_close(c.float(), ref, rtol=2e-2, atol=2e-2 * K ** 0.5)
+    assert gemm_error_code("cuda") == 0
+
+
+def test_b_transposed_batched_ns_layout():
+    """Per-NS-token weights [T, K, N] applied transposed to strided NS rows."""
+    from primus_dlrm_b200.ops.dense import tc_gemm
+    Bsz, T, n_s, K, N = 300, 40, 24, 768, 256
+    x = _bf(Bsz, T, K)
+    w = _bf(T - n_s, K, N)
+    y = torch.zeros(Bsz, T, N, device="cuda", dtype=torch.bfloat16)
+    tc_gemm(x[:, n_s:].transpose(0, 1), w, y[:, n_s:].transpose(0, 1), b_kn=True)
+    ref = torch.einsum("btk,tkn->btn", x[:, n_s:].float(), w.float())
+    torch.testing.assert_close(y[:, n_s:].float(), ref, rtol=2e-2, atol=0.6)
+    assert torch.all(y[:, :n_s] == 0)
+
+
 def test_batched_strided_ns_layout():
     """NS rows of every sample as one batch per token (row stride T*K, batch stride K)."""
     from primus_dlrm_b200.ops.dense import tc_gemm
