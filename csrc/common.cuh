@@ -101,6 +101,12 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+__device__ __forceinline__ float exp2f_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // GELU(x) = x * Phi(x) (the exact, erf-based form used by nn.GELU()).
 // erf is evaluated with Abramowitz & Stegun, Handbook of Mathematical
 // Functions (1964), formula 7.1.26: erf(x) = 1 - (a1 t + ... + a5 t^5) e^{-x^2},
@@ -109,17 +115,19 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // reciprocal and one exponential cover both.
 struct GeluEval { float cdf, pdf; };
 __device__ __forceinline__ GeluEval gelu_eval(float x) {
-  const float z = fabsf(x) * 0.70710678118654752f;               // |x| / sqrt(2)
-  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
-  float poly = fmaf(1.061405429f, t, -1.453152027f);
-  poly = fmaf(poly, t, 1.421413741f);
-  poly = fmaf(poly, t, -0.284496736f);
-  poly = fmaf(poly, t, 0.254829592f);
+  // z = |x| / sqrt(2); p z and -z^2 are formed from |x| with the constants folded
+  const float ax = fabsf(x);
+  const float t = __fdividef(1.0f, fmaf(0.23164188826636045f, ax, 1.0f));   // 1 / (1 + p z)
+  // (a1 t + ... + a5 t^5) / 2: the A&S coefficients halved (exact in binary)
+  float poly = fmaf(0.5307027145f, t, -0.7265760135f);
+  poly = fmaf(poly, t, 0.7107068705f);
+  poly = fmaf(poly, t, -0.142248368f);
+  poly = fmaf(poly, t, 0.127414796f);
   poly *= t;
-  const float e = __expf(-z * z);                                   // exp(-x^2 / 2)
-  const float erf_abs = 1.0f - poly * e;
-  const float erf_v = x < 0.f ? -erf_abs : erf_abs;
-  return GeluEval{0.5f * (1.0f + erf_v), 0.3989422804014327f * e};  // Phi(x), phi(x)
+  const float e = exp2f_approx(ax * ax * -0.72134752044448170f);          // exp(-x^2 / 2)
+  const float half_erf = fmaf(-poly, e, 0.5f);                              // erf(|x| / sqrt 2) / 2
+  const float cdf = 0.5f + copysignf(half_erf, x);                          // Phi(x)
+  return GeluEval{cdf, 0.3989422804014327f * e};                            // Phi(x), phi(x)
 }
 __device__ __forceinline__ float gelu_f(float x) { return x * gelu_eval(x).cdf; }
 __device__ __forceinline__ float gelu_grad_f(float x) {
