@@ -265,10 +265,51 @@ def _native_forward(spec: LookupSpec, ids: list[torch.Tensor], outs: list[torch.
             C.emb_pooled([ids[i] for i in pooled], views, meta, offs, weights, ptrs, tmeta, dim, spec.err)
 
 
-def _native_backward(spec: LookupSpec, ids: list[torch.Tensor], grads: list[torch.Tensor]) -> None:
+class _LocalPlan:
+    """Sorted keys of one embedding dim's slots, made in the forward and reused
+    by the backward (one sort per step)."""
+
+    def __init__(self, dim, sidx, skeys, perm):
+        self.dim, self.sidx, self.skeys, self.perm = dim, sidx, skeys, perm
+
+
+def _native_forward_planned(spec: LookupSpec, ids: list[torch.Tensor], outs: list[torch.Tensor]):
+    """Unpooled lookups on local tables through the deduplicated gather: keys
+    sorted once (the backward reuses the sort), each unique row read once in
+    address order, then expanded to every position.  Returns the plans, or
+    None when a pooled slot makes the direct gather the path."""
+    if any(sl.pool for sl in spec.slots):
+        _native_forward(spec, ids, outs)
+        return None
+    C = _ext.core()
+    plans = []
+    for dim, sidx in _by_dim(spec).items():
+        tables, remap = _launch_tables(spec, sidx)
+        weights = [t.weight for t in tables]
+        ptrs = [t.device_ptrs() for t in tables]
+        tmeta = _table_meta(tables)
+        slot_ids = [ids[i].reshape(-1) for i in sidx]
+        views = [_slot_view(outs[spec.slots[i].group], spec.slots[i].col, dim) for i in sidx]
+        meta4 = torch.tensor([[remap[spec.slots[i].table], 0, 0, -1] for i in sidx], dtype=torch.int64)
+        offs = [ids[i].new_empty(0, dtype=torch.int64) for i in sidx]
+        keys = C.emb_keys(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
+        skeys, perm = torch.sort(keys)
+        n = skeys.numel()
+        first = torch.ones(n, dtype=torch.bool, device=skeys.device)
+        if n > 1:
+            torch.ne(skeys[1:], skeys[:-1], out=first[1:])
+        seg = torch.cumsum(first, 0) - 1
+        uniq = torch.empty_like(skeys).scatter_(0, seg, skeys)
+        C.emb_gather_planned(slot_ids, views, meta4, weights, ptrs, tmeta, dim, skeys, perm, seg, uniq, spec.err)
+        plans.append(_LocalPlan(dim, sidx, skeys, perm))
+    return plans
+
+
+def _native_backward(spec: LookupSpec, ids: list[torch.Tensor], grads: list[torch.Tensor], plans=None) -> None:
     C = _ext.core()
     opt = spec.optimizer
     bc1, bc2 = opt.bias_corrections()
+    planned = {p.dim: p for p in plans} if plans else {}
     for dim, sidx in _by_dim(spec).items():
         tables, remap = _launch_tables(spec, sidx)
         weights = [t.weight for t in tables]
@@ -291,8 +332,12 @@ def _native_backward(spec: LookupSpec, ids: list[torch.Tensor], grads: list[torc
             offs.append(sl.offsets if sl.offsets is not None else ids[i].new_empty(0, dtype=torch.int64))
         meta4 = torch.tensor(meta4, dtype=torch.int64)
         meta5 = torch.tensor(meta5, dtype=torch.int64)
-        keys = C.emb_keys(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
-        skeys, perm = torch.sort(keys)
+        plan = planned.get(dim)
+        if plan is not None and plan.sidx == sidx:
+            skeys, perm = plan.skeys, plan.perm
+        else:
+            keys = C.emb_keys(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
+            skeys, perm = torch.sort(keys)
         scale = grow = None
         if any_pooled:
             scale, grow = C.emb_pooled_scale(slot_ids, views, meta4, offs, weights, ptrs, tmeta, dim)
@@ -343,7 +388,7 @@ class GroupedLookup(torch.autograd.Function):
         if spec.executor is not None:
             plan = spec.executor.forward(spec, list(ids), outs, backward=not isinstance(ctx, _NoCtx))
         elif spec.native:
-            _native_forward(spec, list(ids), outs)
+            plan = _native_forward_planned(spec, list(ids), outs)
         else:
             for i, sl in enumerate(spec.slots):
                 t = spec.tables[sl.table]
@@ -372,7 +417,8 @@ class GroupedLookup(torch.autograd.Function):
                 spec.executor.backward(spec, ids, gs, plan=ctx.exchange_plan)
                 ctx.exchange_plan = None
             elif spec.native:
-                _native_backward(spec, ids, gs)
+                _native_backward(spec, ids, gs, ctx.exchange_plan)
+                ctx.exchange_plan = None
             else:
                 _eager_backward(spec, ids, gs)
         return (None, None) + (None,) * len(ids)
