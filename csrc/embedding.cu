@@ -176,7 +176,7 @@ template <typename OutT>
 __global__ void __launch_bounds__(256) gather_unique_kernel(const __grid_constant__ GatherParams P,
                                                             const int64_t* __restrict__ uniq,
                                                             const int64_t* __restrict__ seg, int64_t n,
-                                                            OutT* __restrict__ stage) {
+                                                            OutT* __restrict__ stage, int* err) {
   const int64_t U = seg[n - 1] + 1;
   const int nvec = P.dim >> 2;
   const int lanes = nvec < 32 ? nvec : 32;
@@ -196,7 +196,8 @@ __global__ void __launch_bounds__(256) gather_unique_kernel(const __grid_constan
       src[u] = nullptr;
       if (r < U) {
         bool ok;
-        src[u] = key_row(P, uniq[r], ok);   // the padding key resolves to no row: zeros
+        src[u] = key_row(P, uniq[r], ok);   // an out-of-range id's key resolves to no row: zeros
+        if (!ok && sub == 0) set_error(err, kIdOutOfRange);
       }
     }
     for (int v = sub; v < nvec; v += lanes) {
@@ -219,14 +220,21 @@ __global__ void __launch_bounds__(256) gather_unique_kernel(const __grid_constan
   }
 }
 
-// out[perm[p]] = stage[seg[p]]: a group of threads per sorted position, rows
-// moved as 16-byte vectors, kGatherUnroll positions in flight per group.
+// Unique index of every position: u_of_pos[perm[p]] = seg[p].
+__global__ void unique_of_position_kernel(const int64_t* __restrict__ perm, const int64_t* __restrict__ seg,
+                                          int32_t* __restrict__ u_of_pos, int64_t n) {
+  for (int64_t p = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; p < n; p += int64_t(gridDim.x) * blockDim.x)
+    u_of_pos[perm[p]] = int32_t(seg[p]);
+}
+
+// out[j] = stage[u_of_pos[j]] in position order: the output rows are written
+// in sequence (the random side is the staged rows, whose hot Zipf entries
+// stay in L2). A group of threads per position, rows moved as 16-byte
+// vectors, kGatherUnroll positions in flight per group.
 template <typename OutT>
 __global__ void __launch_bounds__(256) expand_kernel(const __grid_constant__ GatherParams P,
                                                      const OutT* __restrict__ stage,
-                                                     const int64_t* __restrict__ skeys,
-                                                     const int64_t* __restrict__ seg,
-                                                     const int64_t* __restrict__ perm, int64_t n, int* err) {
+                                                     const int32_t* __restrict__ u_of_pos, int64_t n) {
   const int nvec = int(P.dim * sizeof(OutT) / 16);
   const int lanes = nvec < 32 ? nvec : 32;
   const int groups_per_warp = 32 / lanes;
@@ -237,24 +245,19 @@ __global__ void __launch_bounds__(256) expand_kernel(const __grid_constant__ Gat
   const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
   const int64_t stride = n_warps * groups_per_warp;
-  for (int64_t p0 = warp_global * groups_per_warp + grp; p0 < n; p0 += stride * kGatherUnroll) {
+  for (int64_t j0 = warp_global * groups_per_warp + grp; j0 < n; j0 += stride * kGatherUnroll) {
     const uint4* src[kGatherUnroll];
     uint4* dst[kGatherUnroll];
 #pragma unroll
     for (int u = 0; u < kGatherUnroll; ++u) {
-      const int64_t p = p0 + u * stride;
+      const int64_t j = j0 + u * stride;
       src[u] = nullptr;
       dst[u] = nullptr;
-      if (p < n) {
-        const int64_t j = perm[p];
+      if (j < n) {
         const int s = find_slot(P.slot_off, P.n_slots, j);
         const Slot& sl = P.slots[s];
         dst[u] = reinterpret_cast<uint4*>(static_cast<OutT*>(sl.io) + (j - P.slot_off[s]) * sl.io_stride);
-        if (skeys[p] != INT64_MAX) {
-          src[u] = reinterpret_cast<const uint4*>(stage + seg[p] * P.dim);
-        } else if (sub == 0) {
-          set_error(err, kIdOutOfRange);      // unpooled slots: only an out-of-range id has no key
-        }
+        src[u] = reinterpret_cast<const uint4*>(stage + int64_t(u_of_pos[j]) * P.dim);
       }
     }
     for (int v = sub; v < nvec; v += lanes) {
@@ -841,6 +844,8 @@ void emb_gather_planned(std::vector<at::Tensor> ids, std::vector<at::Tensor> out
                 "planned gather: output rows must be 16-byte aligned");
   }
   auto stage = at::empty({total, dim}, outs[0].options());   // unique rows <= positions
+  TORCH_CHECK(total < (int64_t(1) << 31), "planned gather: more than 2^31 positions in one launch");
+  auto u_of_pos = at::empty({total}, skeys.options().dtype(at::kInt));
   const int nvec = P.dim / 4;
   const int rows_per_warp = nvec < 32 ? 32 / nvec : 1;
   const int64_t blocks = grid_for((total + 8 * rows_per_warp - 1) / (8 * rows_per_warp), 1);
@@ -849,17 +854,21 @@ void emb_gather_planned(std::vector<at::Tensor> ids, std::vector<at::Tensor> out
   const int64_t* pm = perm.data_ptr<int64_t>();
   const int64_t* sg = seg.data_ptr<int64_t>();
   const int64_t* uq = uniq.data_ptr<int64_t>();
+  (void)sk;
+  int32_t* up = u_of_pos.data_ptr<int32_t>();
+  unique_of_position_kernel<<<grid_for(total, 256), 256, 0, s>>>(pm, sg, up, total);
+  PD_CHECK_LAUNCH();
   if (out_t == at::kBFloat16) {
     auto* st = reinterpret_cast<__nv_bfloat16*>(stage.data_ptr());
-    gather_unique_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(P, uq, sg, total, st);
+    gather_unique_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(P, uq, sg, total, st, err.data_ptr<int>());
     PD_CHECK_LAUNCH();
-    expand_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(P, st, sk, sg, pm, total, err.data_ptr<int>());
+    expand_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(P, st, up, total);
   } else {
     TORCH_CHECK(out_t == at::kFloat, "planned gather: bf16 or fp32 outputs");
     auto* st = stage.data_ptr<float>();
-    gather_unique_kernel<float><<<blocks, 256, 0, s>>>(P, uq, sg, total, st);
+    gather_unique_kernel<float><<<blocks, 256, 0, s>>>(P, uq, sg, total, st, err.data_ptr<int>());
     PD_CHECK_LAUNCH();
-    expand_kernel<float><<<blocks, 256, 0, s>>>(P, st, sk, sg, pm, total, err.data_ptr<int>());
+    expand_kernel<float><<<blocks, 256, 0, s>>>(P, st, up, total);
   }
   PD_CHECK_LAUNCH();
 }

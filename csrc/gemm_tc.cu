@@ -563,6 +563,185 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Weight gradient: C[l] (fp32, [M, N]) += sum over rows k of A[l][k, m] B[l][k, n]
+// with A = dY [rows, M] and B = X [rows, N] both stored row-major, i.e. both
+// operands MN-major (no transposes). The row dimension is long (every token of
+// the batch) and the output small, so the work is split over K: a work item
+// is (tile, k-range); items cycle over tiles first so concurrent CTAs hit
+// different outputs. The epilogue adds its fp32 partial tile into C with
+// vector reductions (red.global.add.v4.f32); C must be zeroed by the caller.
+// Warp roles, TMEM double buffering and the bounded waits are those of
+// gemm_kernel.
+// ---------------------------------------------------------------------------
+struct WgParams {
+  int M, N, K, L;
+  int m_blocks, n_blocks, k_blocks, tiles, splits, kb_per_split, items;
+  float* C; int64_t c_ls, c_ms;
+  int a_mode, b_mode;
+  int* err;
+};
+
+__device__ __forceinline__ void wg_item(const WgParams& p, int w, int& l, int& mb, int& nb, int& kb0, int& kb1) {
+  const int t = w % p.tiles;
+  const int sp = w / p.tiles;
+  nb = t % p.n_blocks;
+  const int r = t / p.n_blocks;
+  mb = r % p.m_blocks;
+  l = r / p.m_blocks;
+  kb0 = sp * p.kb_per_split;
+  kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+}
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                            const __grid_constant__ CUtensorMap tmB,
+                                                            const WgParams p) {
+  constexpr uint32_t kABytes = BM * BK * 2;
+  constexpr uint32_t kBBytes = BN * BK * 2;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * kBBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;     // [2]
+  uint64_t* tempty = tfull + 2;         // [2]
+  uint64_t* mma_done = tempty + 2;      // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], kEpiWarps * 32); }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(tmem_slot)), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer: [64 k-rows][64 cols] boxes ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 1;
+      int issued_on[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) issued_on[s] = 0;
+      for (int w = blockIdx.x; w < p.items && !*abort_flag; w += gridDim.x) {
+        int l, mb, nb, kb0, kb1;
+        wg_item(p, w, l, mb, nb, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase, p.err)) { *abort_flag = 1; break; }
+          mbar_expect_tx(&full[stage], kABytes + kBBytes);
+#pragma unroll
+          for (int g = 0; g < BM / 64; ++g)
+            tma_load_rows(sA + stage * kABytes + g * 8192, &tmA, &full[stage], p.a_mode, mb * BM + 64 * g, kb * BK, l);
+#pragma unroll
+          for (int g = 0; g < BN / 64; ++g)
+            tma_load_rows(sB + stage * kBBytes + g * 8192, &tmB, &full[stage], p.b_mode, nb * BN + 64 * g, kb * BK, l);
+          ++issued_on[stage];
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (*abort_flag) {
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s)
+          if (issued_on[s] > 0) (void)mbar_wait(&full[s], uint32_t(issued_on[s] - 1) & 1u, p.err);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (A and B MN-major) ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(BM, BN) | (1u << 15) | (1u << 16);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int w = blockIdx.x; w < p.items && !*abort_flag; w += gridDim.x, ++local) {
+        int l, mb, nb, kb0, kb1;
+        wg_item(p, w, l, mb, nb, kb0, kb1);
+        const int a = local & 1;
+        const uint32_t ephase = ((local >> 1) & 1) ^ 1;
+        if (!mbar_wait(&tempty[a], ephase, p.err)) { *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t d = tmem + uint32_t(a * BN);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) { *abort_flag = 1; ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * kBBytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            tc_mma(d, smem_desc_mn(a_addr + k * 2048), smem_desc_mn(b_addr + k * 2048), idesc,
+                   (kb > kb0 || k > 0) ? 1u : 0u);
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[a]);
+      }
+      tc_commit(mma_done);
+      (void)mbar_wait(mma_done, 0, p.err);
+    }
+  } else {
+    // ---------------- epilogue: fp32 partial tile added into C ----------------
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int part = ew >> 2;
+    constexpr int kParts = kEpiWarps / 4;
+    int local = 0;
+    for (int w = blockIdx.x; w < p.items; w += gridDim.x, ++local) {
+      const int a = local & 1;
+      if (!mbar_wait(&tfull[a], (local >> 1) & 1, p.err)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      int l, mb, nb, kb0, kb1;
+      wg_item(p, w, l, mb, nb, kb0, kb1);
+      const int row = mb * BM + q * 32 + lane;
+      const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t(a * BN);
+#pragma unroll 1
+      for (int c = part * 32; c < BN; c += kParts * 32) {
+        uint32_t r[32];
+        tc_ld32_issue(tbase + c, r);
+        tc_ld_wait(r);
+        if (row < p.M && kb1 > kb0) {
+          float* dst = p.C + l * p.c_ls + int64_t(row) * p.c_ms + nb * BN + c;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            red_add_v4(dst + j, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                       __uint_as_float(r[j + 3]));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[a]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
 }  // namespace tc
 
 // ---------------------------------------------------------------------------
@@ -713,6 +892,50 @@ void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optiona
   if (BN == 256) launch<256, 3>(ta, tb, tcm, txm, trm, p);
   else if (BN == 128) launch<128, 4>(ta, tb, tcm, txm, trm, p);
   else launch<64, 6>(ta, tb, tcm, txm, trm, p);
+}
+
+
+// C[l] (fp32 [M, N], zeroed by the caller) += A[l]^T B[l] over the rows:
+// A [L, K, M], B [L, K, N] bf16 views with unit stride on the last dim.
+void tc_wgrad(at::Tensor A, at::Tensor B, at::Tensor C, at::Tensor err) {
+  check_operand(A, "A");
+  check_operand(B, "B");
+  const int64_t L = A.size(0), K = A.size(1), M = A.size(2), N = B.size(2);
+  TORCH_CHECK(B.size(0) == L && B.size(1) == K, "B must be [L, K, N] over the same rows as A");
+  TORCH_CHECK(M % 64 == 0 && N % 64 == 0, "wgrad: M and N must be multiples of 64");
+  TORCH_CHECK(C.scalar_type() == at::kFloat && C.dim() == 3 && C.size(0) == L && C.size(1) == M && C.size(2) == N &&
+                  C.stride(2) == 1 && C.stride(1) % 4 == 0 && (L == 1 || C.stride(0) % 4 == 0) &&
+                  reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0,
+              "wgrad: C must be an fp32 [L, M, N] view with 16-byte aligned rows");
+  if (K == 0 || L == 0) return;
+  tc::WgParams p{};
+  p.M = int(M); p.N = int(N); p.K = int(K); p.L = int(L);
+  p.m_blocks = int((M + tc::BM - 1) / tc::BM);
+  const int BN = (N % 256 == 0) ? 256 : (N % 128 == 0 ? 128 : 64);
+  p.n_blocks = int(N / BN);
+  p.k_blocks = int((K + tc::BK - 1) / tc::BK);
+  p.tiles = int(L) * p.m_blocks * p.n_blocks;
+  // about two items per SM, each at least 8 k-blocks long
+  int splits = std::max(1, (2 * num_sms() + p.tiles - 1) / p.tiles);
+  splits = std::min(splits, std::max(1, p.k_blocks / 8));
+  p.kb_per_split = (p.k_blocks + splits - 1) / splits;
+  p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+  p.items = p.tiles * p.splits;
+  p.C = C.data_ptr<float>(); p.c_ls = C.stride(0); p.c_ms = C.stride(1);
+  p.err = err.data_ptr<int>();
+  // MN-major operands: [64 k-rows][64 cols] boxes over dims {cols, rows, L}
+  const CUtensorMap ta = make_map(A.data_ptr(), M, K, L, A.stride(1), A.stride(0), tc::BK, p.a_mode);
+  const CUtensorMap tb = make_map(B.data_ptr(), N, K, L, B.stride(1), B.stride(0), tc::BK, p.b_mode);
+  auto go = [&](auto kern, int bn, int stages) {
+    const size_t smem = size_t(stages) * (tc::BM * tc::BK * 2 + bn * tc::BK * 2) + 1024 + 1024;
+    PD_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    const int grid = p.items < num_sms() ? p.items : num_sms();
+    kern<<<grid, tc::kThreads, smem, stream()>>>(ta, tb, p);
+  };
+  if (BN == 256) go(tc::wgrad_kernel<256, 4>, 256, 4);
+  else if (BN == 128) go(tc::wgrad_kernel<128, 6>, 128, 6);
+  else go(tc::wgrad_kernel<64, 8>, 64, 8);
+  PD_CHECK_LAUNCH();
 }
 
 }  // namespace pd

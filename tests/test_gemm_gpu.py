@@ -48,6 +48,27 @@ def test_b_transposed_batched_ns_layout():
     assert torch.all(y[:, :n_s] == 0)
 
 
+@pytest.mark.parametrize("rows,M,N", [(5000, 768, 256), (1000, 256, 1024), (777, 128, 384), (64, 64, 64)])
+def test_wgrad_split_k(rows, M, N):
+    """C = A^T B over the rows (weight gradient), both operands as stored."""
+    from primus_dlrm_b200.ops.dense import gemm_error_code, tc_wgrad
+    a, b = _bf(1, rows, M), _bf(1, rows, N)
+    c = tc_wgrad(a, b, torch.zeros(1, M, N, device="cuda"))
+    ref = a[0].float().t() @ b[0].float()
+    torch.testing.assert_close(c[0], ref, rtol=1e-3, atol=1e-3 * rows ** 0.5)
+    assert gemm_error_code("cuda") == 0
+
+
+def test_wgrad_per_token_strided():
+    """Per-NS-token weight gradients over strided views (one batch per token)."""
+    from primus_dlrm_b200.ops.dense import tc_wgrad
+    Bsz, T, n_s, M, N = 600, 40, 24, 256, 768
+    dy, x = _bf(Bsz, T, M), _bf(Bsz, T, N)
+    c = tc_wgrad(dy[:, n_s:].transpose(0, 1), x[:, n_s:].transpose(0, 1), torch.zeros(T - n_s, M, N, device="cuda"))
+    ref = torch.einsum("btm,btn->tmn", dy[:, n_s:].float(), x[:, n_s:].float())
+    torch.testing.assert_close(c, ref, rtol=1e-3, atol=1e-3 * Bsz ** 0.5)
+
+
 def test_batched_strided_ns_layout():
     """NS rows of every sample as one batch per token (row stride T*K, batch stride K)."""
     from primus_dlrm_b200.ops.dense import tc_gemm
