@@ -915,8 +915,8 @@ void tc_wgrad(at::Tensor A, at::Tensor B, at::Tensor C, at::Tensor err) {
   p.n_blocks = int(N / BN);
   p.k_blocks = int((K + tc::BK - 1) / tc::BK);
   p.tiles = int(L) * p.m_blocks * p.n_blocks;
-  // about two items per SM, each at least 8 k-blocks long
-  int splits = std::max(1, (2 * num_sms() + p.tiles - 1) / p.tiles);
+  // about two items per SM without a ragged last wave, each at least 8 k-blocks long
+  int splits = std::max(1, (2 * num_sms()) / p.tiles);
   splits = std::min(splits, std::max(1, p.k_blocks / 8));
   p.kb_per_split = (p.k_blocks + splits - 1) / splits;
   p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
