@@ -16,6 +16,10 @@ Shapes (rows = batch x tokens):
   dgelu_pre  as ffn_dgrad, GELU' recomputed from the pre-activation
 Times are CUDA-event device times per call after warm-up; each call's
 inputs exceed L2 at the default size.  Bytes count A + B + C (+ R / AUX).
+
+With ``--wgrad`` the weight-gradient products of the same layer (dW = dY^T X
+over all rows, and the per-NS-token ones over the batch) are timed instead:
+the tcgen05 split-K kernel (``tc_wgrad``) against cuBLAS with fp32 output.
 """
 from __future__ import annotations
 
@@ -49,7 +53,10 @@ def main(argv=None) -> list[dict]:
     p.add_argument("--reps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--shapes", default="qkv,ffn_up,ffn_down,ffn_dgrad")
+    p.add_argument("--wgrad", action="store_true")
     a = p.parse_args(argv)
+    if a.wgrad:
+        return _wgrad(a)
     from primus_dlrm_b200.ops.dense import tc_gemm
     peaks = {}
     pk = ROOT / "MEASURED_PEAKS.json"
@@ -85,6 +92,29 @@ def main(argv=None) -> list[dict]:
                "tflops": round(flops / ms / 1e9, 1), "gbs": round(nbytes / ms / 1e6, 1),
                "roofline_ms": round(roof_ms, 4), "frac_of_roofline": round(roof_ms / ms, 3),
                "cublas_plain_ms": round(ref_ms, 4)}
+        out.append(row)
+        print(json.dumps(row), flush=True)
+    return out
+
+
+def _wgrad(a) -> list[dict]:
+    from primus_dlrm_b200.ops.dense import tc_wgrad
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    hbm = float(peaks.get("hbm_gbs", 6650.0)) * 1e9
+    dev = torch.device("cuda")
+    rows, out = a.rows, []
+    for name, M, N in (("qkv", 768, 256), ("ffn_up", 1024, 256), ("ffn_down", 256, 1024), ("out_proj", 256, 256)):
+        A = torch.randn(1, rows, M, device=dev).to(torch.bfloat16)
+        B = torch.randn(1, rows, N, device=dev).to(torch.bfloat16)
+        C = torch.zeros(1, M, N, device=dev)
+        ms = _time(lambda: tc_wgrad(A, B, C), a.reps, a.warmup)
+        ref_ms = _time(lambda: torch.mm(A[0].t(), B[0], out_dtype=torch.float32), a.reps, a.warmup)
+        nbytes = 2.0 * rows * (M + N)
+        row = {"dW": name, "M": M, "N": N, "rows": rows, "tc_ms": round(ms, 4), "cublas_ms": round(ref_ms, 4),
+               "tc_tflops": round(2.0 * rows * M * N / ms / 1e9, 1), "hbm_roofline_ms": round(nbytes / hbm * 1e3, 4)}
         out.append(row)
         print(json.dumps(row), flush=True)
     return out
