@@ -394,20 +394,21 @@ struct GradSrc {
   const int64_t* seg;
 };
 
+template <int KV = 8>
 __device__ __forceinline__ void store_reduced(const GradSrc& src, int64_t q, const float4* acc, int nvec,
                                               int dim, int lane) {
   float4* o = reinterpret_cast<float4*>(src.out_rows + src.seg[q] * int64_t(dim));
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
+  for (int k = 0; k < KV; ++k) {
     const int v = lane + 32 * k;
     if (v < nvec) o[v] = acc[k];
   }
 }
 
-template <typename GradT>
+template <typename GradT, int KV = 8>
 __device__ __forceinline__ void accum_row(float4* acc, const GradT* src, int nvec, int lane, float sc) {
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
+  for (int k = 0; k < KV; ++k) {
     const int v = lane + 32 * k;
     if (v < nvec) {
       float4 x;
@@ -428,6 +429,7 @@ __device__ __forceinline__ int find_table(const GatherParams& P, int64_t key) {
 }
 
 // Apply the optimizer to one row (this rank owns it). acc holds the summed grad.
+template <int KV = 8>
 __device__ void apply_update(const GatherParams& P, const OptParams& O, int64_t key,
                              float4* acc, int nvec, int lane, int* err) {
   const int ti = find_table(P, key);
@@ -436,9 +438,9 @@ __device__ void apply_update(const GatherParams& P, const OptParams& O, int64_t 
   const int64_t r = g - t.local_row0;
   if (r < 0 || r >= t.local_rows) { if (lane == 0) set_error(err, kIdOutOfRange); return; }
   float4* w = reinterpret_cast<float4*>(t.local + r * t.dim);
-  float4 wv[8];
+  float4 wv[KV];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
+  for (int k = 0; k < KV; ++k) {
     const int v = lane + 32 * k;
     wv[k] = v < nvec ? w[v] : make_float4(0.f, 0.f, 0.f, 0.f);
     if (O.weight_decay != 0.f && v < nvec) {
@@ -449,7 +451,7 @@ __device__ void apply_update(const GatherParams& P, const OptParams& O, int64_t 
   if (O.kind == 2) {  // row-wise Adagrad: one accumulator per row, mean of g^2
     float ss = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k)
+    for (int k = 0; k < KV; ++k)
       if (lane + 32 * k < nvec)
         ss += acc[k].x * acc[k].x + acc[k].y * acc[k].y + acc[k].z * acc[k].z + acc[k].w * acc[k].w;
     ss = warp_sum(ss) / float(t.dim);
@@ -458,7 +460,7 @@ __device__ void apply_update(const GatherParams& P, const OptParams& O, int64_t 
     G = __shfl_sync(0xffffffffu, G, 0);
     const float mul = O.lr / (sqrtf(G) + O.eps);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < KV; ++k) {
       const int v = lane + 32 * k;
       if (v < nvec) {
         wv[k].x -= mul * acc[k].x; wv[k].y -= mul * acc[k].y;
@@ -469,7 +471,7 @@ __device__ void apply_update(const GatherParams& P, const OptParams& O, int64_t 
     return;
   }
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
+  for (int k = 0; k < KV; ++k) {
     const int v = lane + 32 * k;
     if (v >= nvec) continue;
     float* gp = reinterpret_cast<float*>(&acc[k]);
@@ -604,7 +606,7 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-template <typename GradT>
+template <typename GradT, int KV>
 __global__ void __launch_bounds__(256) reduce_update_staged_kernel(
     const __grid_constant__ GatherParams P, OptParams O, const int64_t* __restrict__ skeys,
     GradSrc src, int64_t total, float* __restrict__ scratch, int* __restrict__ arrivals, int* err) {
@@ -654,18 +656,18 @@ __global__ void __launch_bounds__(256) reduce_update_staged_kernel(
       runs &= runs - 1;
       const int le = runs ? __ffs(runs) - 1 : n_live;
       const int64_t key = __shfl_sync(FULL, myk, ls);
-      float4 acc[8];
+      float4 acc[KV];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = 0; k < KV; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int l = ls; l < le; ++l) {
         const float sc = __shfl_sync(FULL, gs, l);
-        accum_row<GradT>(acc, reinterpret_cast<const GradT*>(wstage + size_t(l) * rb), nvec, lane, sc);
+        accum_row<GradT, KV>(acc, reinterpret_cast<const GradT*>(wstage + size_t(l) * rb), nvec, lane, sc);
       }
       const bool head = ls > 0 || before != key;
       const bool tail = le < cn || after != key;
       if (head && tail) {
-        if (src.out_rows) store_reduced(src, c0 + ls, acc, nvec, P.dim, lane);
-        else apply_update(P, O, key, acc, nvec, lane, err);
+        if (src.out_rows) store_reduced<KV>(src, c0 + ls, acc, nvec, P.dim, lane);
+        else apply_update<KV>(P, O, key, acc, nvec, lane, err);
       } else {
         const int64_t beg = head ? c0 + ls : lower_bound(skeys, total, key);
         const int64_t end = tail ? c0 + le : lower_bound(skeys, total, key + 1);
@@ -673,7 +675,7 @@ __global__ void __launch_bounds__(256) reduce_update_staged_kernel(
         const int span = int((end - 1) / kChunk - hc + 1);
         float* srow = scratch + hc * int64_t(P.dim);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < KV; ++k) {
           const int v = lane + 32 * k;
           if (v < nvec) {
             atomicAdd(srow + 4 * v + 0, acc[k].x); atomicAdd(srow + 4 * v + 1, acc[k].y);
@@ -688,7 +690,7 @@ __global__ void __launch_bounds__(256) reduce_update_staged_kernel(
         if (prev == span - 1) {
           __threadfence();
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
+          for (int k = 0; k < KV; ++k) {
             const int v = lane + 32 * k;
             if (v < nvec) {
               acc[k] = __ldcg(reinterpret_cast<const float4*>(srow) + v);
@@ -696,8 +698,8 @@ __global__ void __launch_bounds__(256) reduce_update_staged_kernel(
             }
           }
           if (lane == 0) arrivals[hc] = 0;
-          if (src.out_rows) store_reduced(src, beg, acc, nvec, P.dim, lane);
-          else apply_update(P, O, key, acc, nvec, lane, err);
+          if (src.out_rows) store_reduced<KV>(src, beg, acc, nvec, P.dim, lane);
+          else apply_update<KV>(P, O, key, acc, nvec, lane, err);
         }
       }
     }
@@ -1027,8 +1029,14 @@ void emb_reduce_update(std::vector<at::Tensor> grads, at::Tensor slot_meta,
                                                 sc.rows.data_ptr<float>(), sc.arrivals.data_ptr<int>(),
                                                 err.data_ptr<int>());
     };
-    if (gt == at::kBFloat16) launch(reduce_update_staged_kernel<__nv_bfloat16>);
-    else launch(reduce_update_staged_kernel<float>);
+    // accumulators sized to the row: one float4 per lane per 128 columns
+    const int64_t nv = dim / 4;
+    if (gt == at::kBFloat16) {
+      if (nv <= 32) launch(reduce_update_staged_kernel<__nv_bfloat16, 1>);
+      else launch(reduce_update_staged_kernel<__nv_bfloat16, 2>);
+    } else {
+      launch(reduce_update_staged_kernel<float, 1>);   // fp32 rows of at most 512 bytes: dim <= 128
+    }
     PD_CHECK_LAUNCH();
     return;
   }
