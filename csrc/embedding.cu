@@ -232,7 +232,7 @@ __global__ void unique_of_position_kernel(const int64_t* __restrict__ perm, cons
 // stay in L2). A group of threads per position, rows moved as 16-byte
 // vectors, kGatherUnroll positions in flight per group.
 template <typename OutT>
-__global__ void __launch_bounds__(256) expand_kernel(const __grid_constant__ GatherParams P,
+__global__ void __launch_bounds__(256, 4) expand_kernel(const __grid_constant__ GatherParams P,
                                                      const OutT* __restrict__ stage,
                                                      const int32_t* __restrict__ u_of_pos, int64_t n) {
   const int nvec = int(P.dim * sizeof(OutT) / 16);
