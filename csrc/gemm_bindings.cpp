@@ -13,7 +13,7 @@ void fmha_bwd_tc(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int
 int64_t fmha_bwd_tc_max_q();
 void tc_gemm(at::Tensor, at::Tensor, at::Tensor, int64_t, c10::optional<at::Tensor>, c10::optional<at::Tensor>,
              at::Tensor, bool);
-void tc_wgrad(at::Tensor, at::Tensor, at::Tensor, at::Tensor);
+void tc_wgrad(at::Tensor, at::Tensor, at::Tensor, at::Tensor, bool);
 }  // namespace pd
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -28,7 +28,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_gemm", &pd::tc_gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("epi") = 0,
         py::arg("R") = py::none(), py::arg("AUX") = py::none(), py::arg("err"), py::arg("b_kn") = false,
         "C[l] = epi(A[l] @ B[l]^T) on tcgen05 (A [L,M,K], B [L|1,N,K] or with b_kn [L|1,K,N], C [L,M,N] bf16 views)");
-  m.def("tc_wgrad", &pd::tc_wgrad, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("err"),
-        "C[l] (fp32, zeroed) += A[l]^T B[l] over rows on tcgen05, split over rows (A [L,K,M], B [L,K,N] bf16 views)");
+  m.def("tc_wgrad", &pd::tc_wgrad, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("err"), py::arg("l_sum") = false,
+        "C[l] (fp32, zeroed) += A[l]^T B[l] over rows on tcgen05, split over rows (A [L,K,M], B [L,K,N] bf16 views); "
+        "l_sum: one C summed over the batches too");
   m.def("launch_count", &pd::launches);
 }

@@ -578,6 +578,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 struct WgParams {
   int M, N, K, L;
   int m_blocks, n_blocks, k_blocks, tiles, splits, kb_per_split, items;
+  int l_sum;        // 1: the L batches are part of the reduction (one output); k-blocks run over (l, k)
+  int kb_per_l;     // k-blocks of one batch when l_sum
   float* C; int64_t c_ls, c_ms;
   int a_mode, b_mode;
   int* err;
@@ -589,7 +591,7 @@ __device__ __forceinline__ void wg_item(const WgParams& p, int w, int& l, int& m
   nb = t % p.n_blocks;
   const int r = t / p.n_blocks;
   mb = r % p.m_blocks;
-  l = r / p.m_blocks;
+  l = p.l_sum ? 0 : r / p.m_blocks;
   kb0 = sp * p.kb_per_split;
   kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
 }
@@ -652,12 +654,15 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase, p.err)) { *abort_flag = 1; break; }
           mbar_expect_tx(&full[stage], kABytes + kBBytes);
+          // with l_sum a k-block is (batch, block within the batch); rows past a batch's end load as zeros
+          const int lb = p.l_sum ? kb / p.kb_per_l : l;
+          const int kr = (p.l_sum ? kb % p.kb_per_l : kb) * BK;
 #pragma unroll
           for (int g = 0; g < BM / 64; ++g)
-            tma_load_rows(sA + stage * kABytes + g * 8192, &tmA, &full[stage], p.a_mode, mb * BM + 64 * g, kb * BK, l);
+            tma_load_rows(sA + stage * kABytes + g * 8192, &tmA, &full[stage], p.a_mode, mb * BM + 64 * g, kr, lb);
 #pragma unroll
           for (int g = 0; g < BN / 64; ++g)
-            tma_load_rows(sB + stage * kBBytes + g * 8192, &tmB, &full[stage], p.b_mode, nb * BN + 64 * g, kb * BK, l);
+            tma_load_rows(sB + stage * kBBytes + g * 8192, &tmB, &full[stage], p.b_mode, nb * BN + 64 * g, kr, lb);
           ++issued_on[stage];
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -897,14 +902,16 @@ void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optiona
 
 // C[l] (fp32 [M, N], zeroed by the caller) += A[l]^T B[l] over the rows:
 // A [L, K, M], B [L, K, N] bf16 views with unit stride on the last dim.
-void tc_wgrad(at::Tensor A, at::Tensor B, at::Tensor C, at::Tensor err) {
+// With l_sum, C is [1, M, N] and the sum runs over the batches as well.
+void tc_wgrad(at::Tensor A, at::Tensor B, at::Tensor C, at::Tensor err, bool l_sum) {
   check_operand(A, "A");
   check_operand(B, "B");
   const int64_t L = A.size(0), K = A.size(1), M = A.size(2), N = B.size(2);
   TORCH_CHECK(B.size(0) == L && B.size(1) == K, "B must be [L, K, N] over the same rows as A");
   TORCH_CHECK(M % 64 == 0 && N % 64 == 0, "wgrad: M and N must be multiples of 64");
-  TORCH_CHECK(C.scalar_type() == at::kFloat && C.dim() == 3 && C.size(0) == L && C.size(1) == M && C.size(2) == N &&
-                  C.stride(2) == 1 && C.stride(1) % 4 == 0 && (L == 1 || C.stride(0) % 4 == 0) &&
+  const int64_t LC = l_sum ? 1 : L;
+  TORCH_CHECK(C.scalar_type() == at::kFloat && C.dim() == 3 && C.size(0) == LC && C.size(1) == M && C.size(2) == N &&
+                  C.stride(2) == 1 && C.stride(1) % 4 == 0 && (LC == 1 || C.stride(0) % 4 == 0) &&
                   reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0,
               "wgrad: C must be an fp32 [L, M, N] view with 16-byte aligned rows");
   if (K == 0 || L == 0) return;
@@ -913,8 +920,10 @@ void tc_wgrad(at::Tensor A, at::Tensor B, at::Tensor C, at::Tensor err) {
   p.m_blocks = int((M + tc::BM - 1) / tc::BM);
   const int BN = (N % 256 == 0) ? 256 : (N % 128 == 0 ? 128 : 64);
   p.n_blocks = int(N / BN);
-  p.k_blocks = int((K + tc::BK - 1) / tc::BK);
-  p.tiles = int(L) * p.m_blocks * p.n_blocks;
+  p.l_sum = l_sum ? 1 : 0;
+  p.kb_per_l = int((K + tc::BK - 1) / tc::BK);
+  p.k_blocks = l_sum ? int(L) * p.kb_per_l : p.kb_per_l;
+  p.tiles = int(LC) * p.m_blocks * p.n_blocks;
   // about two items per SM without a ragged last wave, each at least 8 k-blocks long
   int splits = std::max(1, (2 * num_sms()) / p.tiles);
   splits = std::min(splits, std::max(1, p.k_blocks / 8));

@@ -65,11 +65,13 @@ def tc_gemm(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, epi: str | None =
     return C
 
 
-def tc_wgrad(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor) -> torch.Tensor:
+def tc_wgrad(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, l_sum: bool = False) -> torch.Tensor:
     """C[l] (fp32 [M, N], zeroed) += A[l]^T B[l] summed over the rows on the
     tcgen05 kernel: A [L, K, M], B [L, K, N] bf16 views (the output gradient
-    and the input of a projection, both as stored)."""
-    _ext.gemm().tc_wgrad(A, B, C, _err(A.device))
+    and the input of a projection, both as stored).  With ``l_sum`` C is
+    [1, M, N] and the sum runs over the L batches too (e.g. the samples of a
+    strided per-sample token range)."""
+    _ext.gemm().tc_wgrad(A, B, C, _err(A.device), l_sum)
     return C
 
 

@@ -69,6 +69,16 @@ def test_wgrad_per_token_strided():
     torch.testing.assert_close(c, ref, rtol=1e-3, atol=1e-3 * Bsz ** 0.5)
 
 
+def test_wgrad_sum_over_samples():
+    """One weight gradient summed over the samples of a strided token range."""
+    from primus_dlrm_b200.ops.dense import tc_wgrad
+    Bsz, T, off, L, M, N = 300, 100, 20, 64, 256, 256
+    dx, h = _bf(Bsz, T, M), _bf(Bsz, L, N)
+    c = tc_wgrad(dx[:, off:off + L], h, torch.zeros(1, M, N, device="cuda"), l_sum=True)
+    ref = torch.einsum("blm,bln->mn", dx[:, off:off + L].float(), h.float())
+    torch.testing.assert_close(c[0], ref, rtol=1e-3, atol=1e-3 * (Bsz * L) ** 0.5)
+
+
 def test_batched_strided_ns_layout():
     """NS rows of every sample as one batch per token (row stride T*K, batch stride K)."""
     from primus_dlrm_b200.ops.dense import tc_gemm
