@@ -146,6 +146,8 @@ class PeerGradSync(_PeerDense):
 
     def __init__(self, numel: int, device: torch.device, group=None, timeout_s: float = 60.0):
         super().__init__(numel, device, group, timeout_s)
+        self._side = None
+        self._pending = False
 
     def bind(self, flat) -> None:
         self.buf.copy_(flat.grad)
@@ -159,6 +161,34 @@ class PeerGradSync(_PeerDense):
         self.all_gather()
         if flat_grad.data_ptr() != self.buf.data_ptr():
             flat_grad.copy_(self.buf)
+
+    # -- overlap with the sparse exchange ---------------------------------
+    def start_async(self, flat_grad: torch.Tensor) -> bool:
+        """Start the all-reduce on a side stream once every dense gradient is
+        final (the embedding lookup's backward runs last, after all of them),
+        so it overlaps the sparse exchange on the compute stream. Returns
+        False (nothing started) when the arena is not the shared buffer."""
+        if self._pending:
+            return True                       # already started this step
+        if flat_grad.data_ptr() != self.buf.data_ptr() or not flat_grad.is_cuda:
+            return False
+        main = torch.cuda.current_stream(flat_grad.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(flat_grad.device)
+        self._side.wait_stream(main)
+        with torch.cuda.stream(self._side):
+            self.reduce_scatter(1.0 / self.world)
+            self.all_gather()
+        self._pending = True
+        return True
+
+    def finish_async(self) -> bool:
+        """Make the compute stream wait for a started all-reduce; False if none."""
+        if not self._pending:
+            return False
+        torch.cuda.current_stream(self.buf.device).wait_stream(self._side)
+        self._pending = False
+        return True
 
 
 class PeerShardedGradSync(_PeerDense):

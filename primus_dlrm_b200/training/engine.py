@@ -13,6 +13,8 @@ This is the step the reference runs in ``DistributedTrainer._sequential_steps``
 """
 from __future__ import annotations
 
+import os
+
 import math
 import time
 
@@ -98,9 +100,17 @@ class TrainEngine:
         self.flat.zero_grad()
         with torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.use_amp):
             total, task_losses = self.compute_loss(batch)
+        ex = self._overlap_executor()
+        if ex is not None:
+            # the dense all-reduce starts when the lookup's backward begins (every
+            # dense gradient is final by then) and runs beside the sparse exchange
+            ex.pre_backward = lambda: self.grad_sync.start_async(self.flat.grad)
         total.backward()
+        if ex is not None:
+            ex.pre_backward = None
         if self.grad_sync is not None:
-            self.grad_sync.sync(self.flat.grad)
+            if not (ex is not None and self.grad_sync.finish_async()):
+                self.grad_sync.sync(self.flat.grad)
         if tc.nan_guard and not bool(torch.isfinite(total)):
             self.skipped_steps += 1
         elif getattr(self.grad_sync, "sharded", False) and isinstance(self.optimizer, FusedAdamW):
@@ -111,6 +121,23 @@ class TrainEngine:
         self.scheduler.step()
         self.global_step += 1
         return total.detach(), task_losses
+
+    def _overlap_executor(self):
+        """The peer exchange executor when the dense sync can overlap it: the
+        model's embedding lookup must be the first op of its forward
+        (``lookup_first``), so its backward runs after every dense gradient
+        has been accumulated."""
+        gs = self.grad_sync
+        if gs is None or os.environ.get("PD_OVERLAP_DENSE_SYNC", "1") == "0":
+            return None
+        inner = self._inner()
+        if not getattr(inner, "lookup_first", False):
+            return None
+        impl = getattr(gs, "impl", None) or gs
+        if not hasattr(impl, "start_async"):
+            return None
+        ex = getattr(getattr(inner, "emb", None), "executor", None)
+        return ex if ex is not None and hasattr(ex, "pre_backward") else None
 
     def step_host(self, packed: PackedBatch) -> float:
         """End-to-end step through the public API: pinned host batch -> H2D
