@@ -26,6 +26,7 @@
 // gets kWaitTimeout, the roles leave their loops, drain their own in-flight
 // copies / MMAs (bounded) and the CTA frees TMEM and exits.
 #include "common.cuh"
+#include "driver_api.h"
 
 #include <cuda.h>
 
@@ -930,7 +931,7 @@ CUtensorMap qkv_map(const at::Tensor& qkv) {
                            cuuint64_t(T * 3 * H * D * 2)};
   cuuint32_t box[5] = {cuuint32_t(D), 1, 1, cuuint32_t(atc::kTile), 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  CUresult r = cuTensorMapEncodeTiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, qkv.data_ptr(), dims, strides, box,
+  CUresult r = tensor_map_encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, qkv.data_ptr(), dims, strides, box,
                                       estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                       D == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -1039,7 +1040,7 @@ void fmha_bwd_tc(at::Tensor qkv, at::Tensor o, at::Tensor lse, at::Tensor dout, 
     cuuint64_t strides[3] = {cuuint64_t(D * 2), cuuint64_t(H * D * 2), cuuint64_t(q_len * H * D * 2)};
     cuuint32_t box[4] = {cuuint32_t(D), 1, cuuint32_t(atc::kTile), 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = cuTensorMapEncodeTiled(&td, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, dout.data_ptr(), dims, strides, box,
+    CUresult r = tensor_map_encode_tiled(&td, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, dout.data_ptr(), dims, strides, box,
                                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                                         CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled(dout) failed: ", int(r));

@@ -14,6 +14,7 @@
 //    %globaltimer) until all peers' epochs arrived in its own pad. On timeout
 //    it records kWaitTimeout in the error word and returns: it never hangs.
 #include "common.cuh"
+#include "driver_api.h"
 
 namespace pd {
 
@@ -40,7 +41,7 @@ at::Tensor ipc_handle(at::Tensor t) {
   TORCH_CHECK(t.is_cuda());
   CUdeviceptr base = 0;
   size_t size = 0;
-  CUresult r = cuMemGetAddressRange(&base, &size, reinterpret_cast<CUdeviceptr>(t.data_ptr()));
+  CUresult r = mem_get_address_range(&base, &size, reinterpret_cast<CUdeviceptr>(t.data_ptr()));
   TORCH_CHECK(r == CUDA_SUCCESS, "cuMemGetAddressRange failed: ", int(r));
   cudaIpcMemHandle_t h;
   PD_CHECK_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));

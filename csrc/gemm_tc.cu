@@ -31,6 +31,7 @@
 // records kWaitTimeout in the error word, stops issuing work, drains its own
 // in-flight operations (bounded) and the CTA frees its TMEM and exits.
 #include "common.cuh"
+#include "driver_api.h"
 
 #include <cuda.h>
 
@@ -774,7 +775,7 @@ CUtensorMap make_map(const void* base, int64_t K, int64_t rows, int64_t L, int64
     box[0] = tc::BK; box[1] = 1; box[2] = box_rows;
   }
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = cuTensorMapEncodeTiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+  CUresult r = tensor_map_encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
                                       box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", int(r), "): K=", K, " rows=", rows, " L=", L,
@@ -802,7 +803,7 @@ CUtensorMap make_store_map(const void* base, int64_t N, int64_t rows, int64_t L,
     box[0] = 32; box[1] = 1; box[2] = 32;
   }
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = cuTensorMapEncodeTiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+  CUresult r = tensor_map_encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
                                       box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                                       CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (store) failed (", int(r), "): N=", N, " rows=", rows,

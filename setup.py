@@ -50,7 +50,6 @@ ext_modules = [
         sources=core_sources,
         include_dirs=[os.path.join(ROOT, "csrc")],
         extra_compile_args={"cxx": CXX, "nvcc": NVCC_COMMON},
-        libraries=["cuda"],
     ),
 ]
 if os.path.exists(os.path.join(ROOT, "csrc", "gemm_bindings.cpp")):
@@ -63,7 +62,6 @@ if os.path.exists(os.path.join(ROOT, "csrc", "gemm_bindings.cpp")):
             "nvcc": NVCC_COMMON + ["-DCUTLASS_ENABLE_TENSOR_CORE_MMA=1", "--use_fast_math",
                                    "-Xptxas=-v" if os.environ.get("PD_PTXAS_V") else "-DPD_NOV"],
         },
-        libraries=["cuda"],
     ))
 
 setup(
