@@ -22,6 +22,8 @@
 // of the fused QKV buffer, zero-filling the Q rows that the pyramid pruned.
 #include "common.cuh"
 
+#include <cstdlib>
+
 namespace pd {
 namespace attn {
 
@@ -107,8 +109,12 @@ struct FwdArgs {
 constexpr int kFwdM = 128;  // queries per CTA (8 warps x 16)
 constexpr int kFwdN = 64;   // keys per tile
 
-template <int D>
-__global__ void __launch_bounds__(256, D == 32 ? 3 : 1) fmha_fwd_kernel(const FwdArgs A) {
+// WARPS warps of 16 query rows each per CTA (8: 128 queries; 4: 64 queries,
+// twice the CTAs, so a barrier stalls half as many warps).
+template <int D, int WARPS = 8>
+__global__ void __launch_bounds__(32 * WARPS, D == 32 ? 24 / WARPS : 1) fmha_fwd_kernel(const FwdArgs A) {
+  constexpr int kFwdM = 16 * WARPS;
+  constexpr int NT = 32 * WARPS;
   constexpr int NKS = D / 16;   // k-steps over d for QK^T
   constexpr int NDT = D / 8;    // n-tiles over d for PV
   __shared__ alignas(128) __nv_bfloat16 sQ[kFwdM * D];
@@ -124,9 +130,9 @@ __global__ void __launch_bounds__(256, D == 32 ? 3 : 1) fmha_fwd_kernel(const Fw
   const int last_key = min(A.kv_len - 1, shift + min(i0 + kFwdM, A.q_len) - 1);
   const int n_tiles = last_key / kFwdN + 1;
 
-  load_tile<D, kFwdM, 256>(sQ, qg, A.q_rs, i0, A.q_len, tid);
-  load_tile<D, kFwdN, 256>(sK[0], kg, A.kv_rs, 0, A.kv_len, tid);
-  load_tile<D, kFwdN, 256>(sV[0], vg, A.kv_rs, 0, A.kv_len, tid);
+  load_tile<D, kFwdM, NT>(sQ, qg, A.q_rs, i0, A.q_len, tid);
+  load_tile<D, kFwdN, NT>(sK[0], kg, A.kv_rs, 0, A.kv_len, tid);
+  load_tile<D, kFwdN, NT>(sV[0], vg, A.kv_rs, 0, A.kv_len, tid);
   cp_async_commit();
 
   // Q fragments (A operand) for this warp's 16 rows
@@ -143,8 +149,8 @@ __global__ void __launch_bounds__(256, D == 32 ? 3 : 1) fmha_fwd_kernel(const Fw
   for (int j = 0; j < n_tiles; ++j) {
     const int buf = j & 1;
     if (j + 1 < n_tiles) {
-      load_tile<D, kFwdN, 256>(sK[buf ^ 1], kg, A.kv_rs, (j + 1) * kFwdN, A.kv_len, tid);
-      load_tile<D, kFwdN, 256>(sV[buf ^ 1], vg, A.kv_rs, (j + 1) * kFwdN, A.kv_len, tid);
+      load_tile<D, kFwdN, NT>(sK[buf ^ 1], kg, A.kv_rs, (j + 1) * kFwdN, A.kv_len, tid);
+      load_tile<D, kFwdN, NT>(sV[buf ^ 1], vg, A.kv_rs, (j + 1) * kFwdN, A.kv_len, tid);
     }
     cp_async_commit();
     cp_async_wait<1>();
@@ -553,9 +559,21 @@ std::vector<at::Tensor> fmha_fwd(at::Tensor q, at::Tensor k, at::Tensor v, doubl
                   reinterpret_cast<const __nv_bfloat16*>(v.data_ptr()), q.stride(0), q.stride(1), k.stride(0), k.stride(1),
                   reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), o.stride(0), o.stride(1), lse.data_ptr<float>(), H, ql, kl,
                   float(scale * 1.4426950408889634)};
-  dim3 grid((ql + attn::kFwdM - 1) / attn::kFwdM, B * H);
-  if (D == 32) attn::fmha_fwd_kernel<32><<<grid, 256, 0, stream()>>>(A);
-  else attn::fmha_fwd_kernel<64><<<grid, 256, 0, stream()>>>(A);
+  // d = 32: 64-query CTAs (4 warps, 6 per SM) by default -- v6 pyramid 18.06 ms
+  // against 21.38 ms with 128-query CTAs and 18.26 ms with 32-query ones;
+  // PD_FMHA_FWD_WARPS=8 selects the 128-query CTAs.
+  static const int warps = [] {
+    const char* e = std::getenv("PD_FMHA_FWD_WARPS");
+    return (e != nullptr && std::atoi(e) == 8) ? 8 : 4;
+  }();
+  if (D == 32 && warps == 4) {
+    dim3 grid4((ql + 63) / 64, B * H);
+    attn::fmha_fwd_kernel<32, 4><<<grid4, 128, 0, stream()>>>(A);
+  } else {
+    dim3 grid((ql + attn::kFwdM - 1) / attn::kFwdM, B * H);
+    if (D == 32) attn::fmha_fwd_kernel<32><<<grid, 256, 0, stream()>>>(A);
+    else attn::fmha_fwd_kernel<64><<<grid, 256, 0, stream()>>>(A);
+  }
   PD_CHECK_LAUNCH();
   return {o, lse};
 }
