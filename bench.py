@@ -26,6 +26,7 @@ import json
 import os
 import statistics
 import subprocess
+import tempfile
 import sys
 import time
 
@@ -72,7 +73,9 @@ class ClockSampler:
     def __init__(self, gpus: list[int]):
         self.gpus = gpus
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        # samples go to PD_CLOCKS_DIR when set (to keep them), else to the temp directory
+        out_dir = os.environ.get("PD_CLOCKS_DIR") or tempfile.gettempdir()
+        self.path = os.path.join(out_dir, f"clocks_{os.getpid()}.csv")
 
     def start(self):
         try:
