@@ -71,6 +71,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err
   }
   return true;
 }
+// Non-blocking probe of an mbarrier phase.
+__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
+  return ok != 0;
+}
 // 5-D tiled TMA load into this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
                                             int c3, int c4) {
@@ -122,6 +132,11 @@ __device__ __forceinline__ void tm_ld_wait(uint32_t* r) {
                  "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
                  "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
                  "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :: "memory");
+}
+__device__ __forceinline__ void tm_ld_wait8(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7])
                :: "memory");
 }
 __device__ __forceinline__ void tm_st32(uint32_t taddr, const uint32_t* r) {
@@ -495,18 +510,25 @@ __global__ void __launch_bounds__(kFwdThreads, 2) fmha_fwd_tc_kernel(const __gri
 // One CTA owns every key tile of the head, so dQ accumulates in shared
 // memory (no fp32 atomics, no accumulator buffer, no conversion pass) and
 // delta = rowsum(dO * O) is computed in the CTA's prologue: one launch.
-// With d = 32 the dV / dK / dQ products are N = 32 MMAs, whose cost is
-// dominated by operand traffic; taking A from TMEM for dV and dK (thread =
-// key row writes P^T / dS^T straight into TMEM lanes) leaves only dQ reading
-// a 4 KB A operand from shared memory.
 //
-// Warps: 0 TMA, 1 TMEM + MMA issuer, 2..17 compute (warp w reads TMEM lanes
-// 32 (w % 4)..+31 = key rows; (w - 2) / 4 selects 32 of the 128 query columns).
+// Issue: a single thread that issues tcgen05.mma back to back waits about
+// 100-120 cycles per instruction whatever N is, while the tensor pipe can
+// take instructions from several warps at once (measured with
+// scripts/bench_tcgen05_mma.py: an N = 32 TS product runs 4x faster from
+// four issuing warps than from one; two lanes of one warp only 1.5x). With
+// d = 32 a pair is 4 N = 128 and 24 N = 32 products, so each product stream
+// has its own issuing warp:
+//   warp 0  S^T and dP^T of the next pair (as soon as the compute warps
+//           have read the current ones), warp 1 dV, warp 2 dK, warp 3 dQ.
+// Warps 4..19 compute (warp w reads TMEM lanes 32 (w % 4)..+31 = key rows;
+// (w - 4) / 4 selects 32 of the 128 query columns). 20 warps keep every
+// sub-partition at 5 warps (96 registers per thread).
+// The TMA loads (QST stages of Q / dO, two of K / V) are issued by lane 0
+// of warp 4: it knows when a buffer is free because it has just waited for
+// the products that read it (mma2_done), so its waits never block on work
+// that itself waits for the compute warps.
 // TMEM (512 columns): S^T [0,128), dP^T [128,256), P^T bf16 [256,320),
 // dS^T bf16 [320,384), dV [384,416), dK [416,448), dQ [448,480).
-// The MMA warp issues the next pair's S^T / dP^T as soon as the compute
-// warps have read the current ones, so the exponentials of pair p + 1
-// overlap the dV / dK / dQ products of pair p.
 // ===========================================================================
 struct BwdArgs {
   int B, H, T, q_len, nq, nkv, items;
@@ -520,34 +542,30 @@ struct BwdArgs {
 };
 
 constexpr int kBwdCompute = 16;                       // compute warps
-constexpr int kBwdThreads = 64 + 32 * kBwdCompute;
+constexpr int kBwdC0 = 4;                             // first compute warp
+constexpr int kBwdThreads = 32 * (kBwdC0 + kBwdCompute);
 constexpr int kBwdCT = 32 * kBwdCompute;              // compute threads
 constexpr int kDbgPairs = 64, kDbgSlots = 16;
 
 // Pair enumeration shared by every role: items (b, h) of this CTA, key tiles,
-// then the query tiles that see the key tile.
+// then the query tiles that see the key tile. Only the cursor lives in
+// registers; the shapes come from the kernel arguments.
 struct PairIt {
-  int w, w_end, jt, i, first_i;
-  int off, nq, nkv;
-  __device__ void first_q() {
-    const int k0 = jt * kTile;
+  int w, jt, i, first_i;
+  __device__ void first_q(const BwdArgs& a) {
+    const int k0 = jt * kTile, off = a.T - a.q_len;
     first_i = k0 > off ? (k0 - off) / kTile : 0;
     i = first_i;
   }
-  __device__ void start(const BwdArgs& a, int wb, int we) {
-    w = wb; w_end = we; off = a.T - a.q_len; nq = a.nq; nkv = a.nkv; jt = 0;
-    first_q();
-  }
-  __device__ bool valid() const { return w < w_end; }
-  __device__ bool last_of_kv() const { return i == nq - 1; }
+  __device__ void start(const BwdArgs& a, int wb) { w = wb; jt = 0; first_q(a); }
+  __device__ bool last_of_kv(const BwdArgs& a) const { return i == a.nq - 1; }
   __device__ bool first_of_kv() const { return i == first_i; }
-  __device__ void next() {
-    if (++i < nq) return;
-    if (++jt < nkv) { first_q(); return; }
-    ++w; jt = 0; first_q();
+  __device__ void next(const BwdArgs& a) {
+    if (++i < a.nq) return;
+    if (++jt < a.nkv) { first_q(a); return; }
+    ++w; jt = 0; first_q(a);
   }
 };
-
 __device__ __forceinline__ void dbg_stamp(const BwdArgs& a, int pc, int slot) {
   if (a.dbg != nullptr && blockIdx.x == 0 && pc < kDbgPairs) a.dbg[pc * kDbgSlots + slot] = clock64();
 }
@@ -556,7 +574,20 @@ __device__ __forceinline__ void tm_ld8(uint32_t taddr, uint32_t* r) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                : "r"(taddr));
 }
+__device__ __forceinline__ void tm_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+// Wait for this thread's tcgen05 work committed to `bar` (bounded).
+__device__ __forceinline__ void drain(uint64_t* bar, int* err) {
+  tc_commit(bar);
+  (void)mbar_wait(bar, 0, err);
+}
 
+template <int QST>
 __global__ void __launch_bounds__(kBwdThreads, 1) fmha_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                                                                     const __grid_constant__ CUtensorMap tm_do,
                                                                     const BwdArgs a) {
@@ -567,39 +598,38 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fmha_bwd_tc_kernel(const __gri
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;                                // [2] key tiles
   uint8_t* sV = sK + 2 * G::kTileBytes;              // [2]
-  uint8_t* sQ = sV + 2 * G::kTileBytes;              // [2] stages
-  uint8_t* sdO = sQ + 2 * G::kTileBytes;             // [2] stages
-  uint8_t* sdS = sdO + 2 * G::kTileBytes;            // 128 x 128 bf16, MN-major SW128 for the dQ product
+  uint8_t* sQ = sV + 2 * G::kTileBytes;              // [QST] stages
+  uint8_t* sdO = sQ + QST * G::kTileBytes;           // [QST] stages
+  uint8_t* sdS = sdO + QST * G::kTileBytes;          // 128 x 128 bf16, MN-major SW128 for the dQ product
   float* sLSE = reinterpret_cast<float*>(sdS + 32768);          // [nq * 128]
   float* sDel = sLSE + a.nq * kTile;                             // [nq * 128]
   float* sdQ = sDel + a.nq * kTile;                              // [q_len(8)] x 32 fp32, 16B chunks swizzled
   const int qrows = (a.q_len + 7) & ~7;
   uint64_t* bar = reinterpret_cast<uint64_t*>(sdQ + qrows * 32);
-  uint64_t* kv_full = bar;          // [2]
-  uint64_t* kv_empty = bar + 2;     // [2]
-  uint64_t* qd_full = bar + 4;      // [2]
-  uint64_t* qd_empty = bar + 6;     // [2]
-  uint64_t* s_full = bar + 8;
-  uint64_t* s_free = bar + 9;
-  uint64_t* p_full = bar + 10;
-  uint64_t* mma2_done = bar + 11;
-  uint64_t* mma_done = bar + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 13);
+  uint64_t* kv_full = bar;               // [2]
+  uint64_t* kv_empty = bar + 2;          // [2]   arrivals: the dQ issuer's commit
+  uint64_t* qd_full = bar + 4;           // [QST]
+  uint64_t* qd_empty = bar + 4 + QST;    // [QST] arrivals: the dV and dK issuers' commits
+  uint64_t* s_full = bar + 4 + 2 * QST;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* mma2_done = s_full + 3;      // arrivals: dV, dK, dQ issuers
+  uint64_t* drained = s_full + 4;        // [4] one per issuing warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int k = 0; k < 2; ++k) {
-      mbar_init(&kv_full[k], 1); mbar_init(&kv_empty[k], 1); mbar_init(&qd_full[k], 1); mbar_init(&qd_empty[k], 1);
-    }
-    mbar_init(s_full, 1); mbar_init(s_free, kBwdCT); mbar_init(p_full, kBwdCT); mbar_init(mma2_done, 1);
-    mbar_init(mma_done, 1);
+    for (int k = 0; k < 2; ++k) { mbar_init(&kv_full[k], 1); mbar_init(&kv_empty[k], 1); }
+    for (int k = 0; k < QST; ++k) { mbar_init(&qd_full[k], 1); mbar_init(&qd_empty[k], 2); }
+    mbar_init(s_full, 1); mbar_init(s_free, kBwdCT); mbar_init(p_full, kBwdCT); mbar_init(mma2_done, 3);
+    for (int k = 0; k < 4; ++k) mbar_init(&drained[k], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_qkv) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_do) : "memory");
   }
-  if (warp == 1) {
+  if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                  ::"r"(smem_u32(tmem_slot)), "r"(512) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -611,126 +641,152 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fmha_bwd_tc_kernel(const __gri
   const int per = (a.items + gridDim.x - 1) / gridDim.x;
   const int w_begin = blockIdx.x * per, w_end = min(a.items, w_begin + per);
   const int off = a.T - a.q_len;
+  // registers: the issuing warpgroup (warps 0-3) needs few, the compute
+  // warpgroups take them (640 x 96 at launch >= 128 x 56 + 512 x 104)
+  if (warp < kBwdC0) asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+  else asm volatile("setmaxnreg.inc.sync.aligned.u32 104;" ::: "memory");
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA loads + S^T / dP^T issuer ----------------
     if (lane == 0) {
-      PairIt it;
-      it.start(a, w_begin, w_end);
-      int pc = 0, kc = 0;
-      int issued_kv[2] = {0, 0}, issued_qd[2] = {0, 0};
-      for (; it.valid() && !*abort_flag; it.next(), ++pc) {
-        const int b = it.w / a.H, h = it.w - (it.w / a.H) * a.H;
-        if (it.first_of_kv()) {
-          const int kb = kc & 1;
-          if (!mbar_wait(&kv_empty[kb], ((kc >> 1) & 1) ^ 1, a.err)) { *abort_flag = 1; break; }
+      constexpr uint32_t id_s = idesc(128, 128, 0, 0);
+      PairIt it, ld;
+      it.start(a, w_begin);
+      ld.start(a, w_begin);
+      int pc = 0, kc = 0;          // pairs issued, key tiles consumed
+      int ldc = 0, kvc = 0;        // pairs loaded, key tiles loaded
+      // Load pair ldc (and its K / V tile when it opens one). A Q / dO stage is
+      // free once the dV / dK products of the pair QST back completed; a K / V
+      // buffer once the dQ products of the tile two back completed. block:
+      // wait for them (bounded); else only issue when both are already free.
+      // Returns 1 issued, 0 not yet free, -1 wait timed out.
+      auto load_one = [&](bool block) -> int {
+        const int lb = ld.w / a.H, lh = ld.w - lb * a.H;
+        const int st = ldc % QST;
+        const uint32_t qpar = uint32_t((ldc / QST) & 1) ^ 1u;
+        const bool opens = ld.first_of_kv();
+        const int kb = kvc & 1;
+        const uint32_t kpar = uint32_t((kvc >> 1) & 1) ^ 1u;
+        if (!block && !(mbar_test(&qd_empty[st], qpar) && (!opens || mbar_test(&kv_empty[kb], kpar)))) return 0;
+        if (opens) {
+          if (!mbar_wait(&kv_empty[kb], kpar, a.err)) return -1;
           mbar_expect_tx(&kv_full[kb], 2 * G::kTileBytes);
-          tma_load_5d(sK + kb * G::kTileBytes, &tm_qkv, &kv_full[kb], 0, h, 1, it.jt * kTile, b);
-          tma_load_5d(sV + kb * G::kTileBytes, &tm_qkv, &kv_full[kb], 0, h, 2, it.jt * kTile, b);
-          ++issued_kv[kb];
-          ++kc;
+          tma_load_5d(sK + kb * G::kTileBytes, &tm_qkv, &kv_full[kb], 0, lh, 1, ld.jt * kTile, lb);
+          tma_load_5d(sV + kb * G::kTileBytes, &tm_qkv, &kv_full[kb], 0, lh, 2, ld.jt * kTile, lb);
+          ++kvc;
         }
-        const int st = pc & 1;
-        if (!mbar_wait(&qd_empty[st], ((pc >> 1) & 1) ^ 1, a.err)) { *abort_flag = 1; break; }
+        if (!mbar_wait(&qd_empty[st], qpar, a.err)) return -1;
         mbar_expect_tx(&qd_full[st], 2 * G::kTileBytes);
-        tma_load_5d(sQ + st * G::kTileBytes, &tm_qkv, &qd_full[st], 0, h, 0, off + it.i * kTile, b);
+        tma_load_5d(sQ + st * G::kTileBytes, &tm_qkv, &qd_full[st], 0, lh, 0, off + ld.i * kTile, lb);
         asm volatile(
             "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
-            "[%2];" ::"r"(smem_u32(sdO + st * G::kTileBytes)), "l"(&tm_do), "r"(smem_u32(&qd_full[st])), "r"(0), "r"(h),
-            "r"(it.i * kTile), "r"(b) : "memory");
-        ++issued_qd[st];
-      }
-      if (*abort_flag) {
-        for (int k = 0; k < 2; ++k) {
-          if (issued_kv[k] > 0) (void)mbar_wait(&kv_full[k], uint32_t(issued_kv[k] - 1) & 1u, a.err);
-          if (issued_qd[k] > 0) (void)mbar_wait(&qd_full[k], uint32_t(issued_qd[k] - 1) & 1u, a.err);
+            "[%2];" ::"r"(smem_u32(sdO + st * G::kTileBytes)), "l"(&tm_do), "r"(smem_u32(&qd_full[st])), "r"(0),
+            "r"(lh), "r"(ld.i * kTile), "r"(lb) : "memory");
+        ld.next(a);
+        ++ldc;
+        return 1;
+      };
+      bool good = true;
+      for (; good && it.w < w_end && !*abort_flag; it.next(a), ++pc) {
+        if (pc > 0) {
+          // wait until the compute warps have read S^T / dP^T of the last pair,
+          // issuing loads as their buffers free up meanwhile
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_test(s_free, uint32_t(pc - 1) & 1u)) {
+            if (ld.w < w_end && ldc < pc + QST && load_one(false) < 0) { good = false; break; }
+            if (globaltimer_ns() - t0 > kWaitLimitNs) { set_error(a.err, kWaitTimeout); good = false; break; }
+            __nanosleep(64);
+          }
+          if (!good) break;
         }
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t id_s = idesc(128, 128, 0, 0);       // S^T, dP^T
-      constexpr uint32_t id_kv = idesc(128, D, 0, 1);        // dV, dK: A in TMEM, B (dO / Q) MN-major
-      constexpr uint32_t id_q = idesc(128, D, 1, 1);         // dQ: A (dS) MN-major, B (K) MN-major
-      PairIt cur;
-      cur.start(a, w_begin, w_end);
-      int pc = 0, kc = 0;          // pair index of `cur`, key tiles seen including cur's
-      bool ok = true;
-      auto issue_s = [&](const PairIt& it, int p, int& kcount) -> bool {
+        dbg_stamp(a, pc, 8);
+        while (ld.w < w_end && ldc <= pc)                        // this pair's loads
+          if (load_one(true) < 0) { good = false; break; }
+        while (good && ld.w < w_end && ldc < pc + QST && load_one(false) == 1) {}
+        if (!good) break;
         if (it.first_of_kv()) {
-          if (!mbar_wait(&kv_full[kcount & 1], (kcount >> 1) & 1, a.err)) return false;
-          ++kcount;
+          if (!mbar_wait(&kv_full[kc & 1], (kc >> 1) & 1, a.err)) { good = false; break; }
+          ++kc;
         }
-        if (!mbar_wait(&qd_full[p & 1], (p >> 1) & 1, a.err)) return false;
+        const int st = pc % QST;
+        if (!mbar_wait(&qd_full[st], (pc / QST) & 1, a.err)) { good = false; break; }
+        dbg_stamp(a, pc, 9);
         tc_fence_after();
-        const int kb = (kcount - 1) & 1;
+        const int kb = (kc - 1) & 1;
         const uint32_t kt = smem_u32(sK + kb * G::kTileBytes), vt = smem_u32(sV + kb * G::kTileBytes);
-        const uint32_t qt = smem_u32(sQ + (p & 1) * G::kTileBytes), dt = smem_u32(sdO + (p & 1) * G::kTileBytes);
+        const uint32_t qt = smem_u32(sQ + st * G::kTileBytes), dt = smem_u32(sdO + st * G::kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) mma_ss(tmem + cS, desc_k<D>(kt, kk), desc_k<D>(qt, kk), id_s, kk > 0);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) mma_ss(tmem + cdP, desc_k<D>(vt, kk), desc_k<D>(dt, kk), id_s, kk > 0);
         tc_commit(s_full);
-        return true;
-      };
-      if (cur.valid()) ok = issue_s(cur, 0, kc);
-      while (ok && cur.valid() && !*abort_flag) {
-        const int kb = (kc - 1) & 1;
-        PairIt nxt = cur;
-        nxt.next();
-        int kc_next = kc;
-        if (nxt.valid()) {
-          if (!mbar_wait(s_free, pc & 1, a.err)) { ok = false; break; }
-          dbg_stamp(a, pc, 8);
-          tc_fence_after();
-          if (!issue_s(nxt, pc + 1, kc_next)) { ok = false; break; }
-          dbg_stamp(a, pc, 10);
-        }
-        if (!mbar_wait(p_full, pc & 1, a.err)) { ok = false; break; }
-        dbg_stamp(a, pc, 11);
-        tc_fence_after();
-        const uint32_t kt = smem_u32(sK + kb * G::kTileBytes);
-        const uint32_t qt = smem_u32(sQ + (pc & 1) * G::kTileBytes), dt = smem_u32(sdO + (pc & 1) * G::kTileBytes);
-        const uint32_t acc0 = cur.first_of_kv() ? 0u : 1u;
-        const uint32_t ds = smem_u32(sdS);
-        // the k-steps of dV, dK and dQ interleaved: consecutive instructions write
-        // different accumulators (1.2 % faster over the v6 pyramid than issuing
-        // the three products one after another)
-#pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-          mma_ts(tmem + cdV, tmem + cP + uint32_t(8 * kk), desc_mn<D>(dt, kk), id_kv, (kk > 0) ? 1u : acc0);
-          mma_ts(tmem + cdK, tmem + cdS + uint32_t(8 * kk), desc_mn<D>(qt, kk), id_kv, (kk > 0) ? 1u : acc0);
-          mma_ss(tmem + cdQ, make_desc(ds + uint32_t(kk) * 2048u, 16384u, 1024u, 2), desc_mn<D>(kt, kk), id_q,
-                 kk > 0 ? 1u : 0u);
-        }
-        dbg_stamp(a, pc, 14);
-        tc_commit(&qd_empty[pc & 1]);
-        if (cur.last_of_kv()) tc_commit(&kv_empty[kb]);
-        tc_commit(mma2_done);
-        dbg_stamp(a, pc, 12);
-        cur = nxt;
-        kc = kc_next;
-        ++pc;
+        dbg_stamp(a, pc, 10);
       }
-      if (!ok) *abort_flag = 1;
-      tc_commit(mma_done);
-      (void)mbar_wait(mma_done, 0, a.err);
+      if (!good) {
+        *abort_flag = 1;
+        // every issued copy lands before the CTA may exit: loads into buffer k
+        // were issued for counts k, k + n, k + 2n, ... below the total
+        for (int k = 0; k < 2; ++k)
+          if (kvc > k) (void)mbar_wait(&kv_full[k], uint32_t((kvc - 1 - k) / 2) & 1u, a.err);
+        for (int k = 0; k < QST; ++k)
+          if (ldc > k) (void)mbar_wait(&qd_full[k], uint32_t((ldc - 1 - k) / QST) & 1u, a.err);
+      }
+      drain(&drained[0], a.err);
+    }
+  } else if (warp < kBwdC0) {
+    // ---------------- dV (warp 1), dK (warp 2), dQ (warp 3) issuers ----------------
+    if (lane == 0) {
+      const int role = warp - 1;
+      constexpr uint32_t id_kv = idesc(128, D, 0, 1);        // A in TMEM, B (dO / Q) MN-major
+      constexpr uint32_t id_q = idesc(128, D, 1, 1);         // A (dS) MN-major, B (K) MN-major
+      PairIt it;
+      it.start(a, w_begin);
+      int pc = 0, kc = 0;
+      const uint32_t ds = smem_u32(sdS);
+      for (; it.w < w_end && !*abort_flag; it.next(a), ++pc) {
+        if (it.first_of_kv()) ++kc;
+        if (!mbar_wait(p_full, pc & 1, a.err)) { *abort_flag = 1; break; }
+        if (role != 1) dbg_stamp(a, pc, role == 0 ? 11 : 14);
+        tc_fence_after();
+        const int st = pc % QST, kb = (kc - 1) & 1;
+        const uint32_t acc0 = it.first_of_kv() ? 0u : 1u;
+        if (role == 0) {
+          const uint32_t dt = smem_u32(sdO + st * G::kTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk)
+            mma_ts(tmem + cdV, tmem + cP + uint32_t(8 * kk), desc_mn<D>(dt, kk), id_kv, (kk > 0) ? 1u : acc0);
+          tc_commit(&qd_empty[st]);
+        } else if (role == 1) {
+          const uint32_t qt = smem_u32(sQ + st * G::kTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk)
+            mma_ts(tmem + cdK, tmem + cdS + uint32_t(8 * kk), desc_mn<D>(qt, kk), id_kv, (kk > 0) ? 1u : acc0);
+          tc_commit(&qd_empty[st]);
+        } else {
+          const uint32_t kt = smem_u32(sK + kb * G::kTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk)
+            mma_ss(tmem + cdQ, make_desc(ds + uint32_t(kk) * 2048u, 16384u, 1024u, 2), desc_mn<D>(kt, kk), id_q,
+                   kk > 0 ? 1u : 0u);
+          if (it.last_of_kv(a)) tc_commit(&kv_empty[kb]);
+        }
+        tc_commit(mma2_done);
+        if (role != 1) dbg_stamp(a, pc, role == 0 ? 12 : 15);
+      }
+      drain(&drained[1 + role], a.err);
     }
   } else {
     // ---------------- compute warps ----------------
-    const int ct = threadIdx.x - 64;                   // 0 .. 511
+    const int ct = threadIdx.x - 32 * kBwdC0;          // 0 .. 511
     const int quarter = warp & 3;
-    const int g = (warp - 2) >> 2;                     // query columns [32 g, 32 g + 32)
+    const int g = (warp - kBwdC0) >> 2;                // query columns [32 g, 32 g + 32)
     const int r = quarter * 32 + lane;                 // key row within the tile = TMEM lane
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
-    const bool stamp = (warp == 2 && lane == 0);
+    const bool stamp = (warp == kBwdC0 && lane == 0);
     auto bar_compute = [&]() { asm volatile("bar.sync 1, %0;" ::"n"(kBwdCT) : "memory"); };
-    // dQ of a finished pair (lanes = query rows, this warp's 8 columns) into the smem block
-    auto add_dq = [&](int qi) {
-      uint32_t qr[8];
-      tm_ld8(lane_base + cdQ + uint32_t(8 * g), qr);
-      tm_ld_wait();
+    // dQ of a finished pair (lanes = query rows, this warp's 8 columns) into
+    // the smem block; `qr` was loaded from TMEM (tm_ld8) and waited for
+    auto add_dq = [&](int qi, const uint32_t* qr) {
       const int qrow = qi * kTile + r;
       if (qrow < a.q_len) {
 #pragma unroll
@@ -768,10 +824,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fmha_bwd_tc_kernel(const __gri
       }
     };
     PairIt it;
-    it.start(a, w_begin, w_end);
+    it.start(a, w_begin);
     int pc = 0;
     bool ok = true;
-    while (it.valid() && ok && !*abort_flag) {
+    while (it.w < w_end && ok && !*abort_flag) {
       const int w = it.w;
       const int b = w / a.H, h = w - (w / a.H) * a.H;
       // ---- prologue: lse, delta = rowsum(dO * O), zero dQ ----
@@ -801,59 +857,80 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fmha_bwd_tc_kernel(const __gri
       bar_compute();
       int prev_i = -1, prev_jt = -1;
       bool prev_last_kv = false;
-      for (; it.valid() && it.w == w; it.next(), ++pc) {
+      for (; it.w < w_end && it.w == w; it.next(a), ++pc) {
         if (stamp) dbg_stamp(a, pc, 0);
         if (!mbar_wait(s_full, pc & 1, a.err)) { ok = false; break; }
         if (stamp) dbg_stamp(a, pc, 1);
         tc_fence_after();
-        uint32_t sr[32], dr[32];
-        tm_ld32(lane_base + cS + uint32_t(32 * g), sr);
-        tm_ld32(lane_base + cdP + uint32_t(32 * g), dr);
-        tm_ld_wait();
-        tc_fence_before();
-        mbar_arrive(s_free);
-        if (stamp) dbg_stamp(a, pc, 2);
-        // P^T, dS^T for key row r, queries q0 + c
+        // P^T, dS^T for key row r, queries q0 + c, in two halves of 16 columns
+        // (the second half's S^T / dP^T are loaded after the first half is
+        // done, which keeps the live registers low); S^T / dP^T are released
+        // to the next pair's products once both halves are in registers
         const int q0 = it.i * kTile + 32 * g;
         const int key = it.jt * kTile + r;
         const int lim = key - off - q0;                    // query column c is visible iff c >= lim
         const int lim_hi = __reduce_max_sync(0xffffffffu, lim);
         const int lim_lo = __reduce_min_sync(0xffffffffu, lim);
         uint32_t pp[16], dd[16];
+        auto half = [&](int h0, const uint32_t* sr, const uint32_t* dr) {
+#pragma unroll
+          for (int c = 0; c < 16; c += 4) {
+            const int cc = h0 + c;
+            const float4 l4 = *reinterpret_cast<const float4*>(sLSE + q0 + cc);
+            const float4 d4 = *reinterpret_cast<const float4*>(sDel + q0 + cc);
+            // columns 12..15 of each half on the FMA pipe: the MUFU unit
+            // (16 ex2 per clock per SM) would otherwise bound the pair
+            const float x0 = fmaf(__uint_as_float(sr[c]), a.c2, -l4.x);
+            const float x1 = fmaf(__uint_as_float(sr[c + 1]), a.c2, -l4.y);
+            const float x2 = fmaf(__uint_as_float(sr[c + 2]), a.c2, -l4.z);
+            const float x3 = fmaf(__uint_as_float(sr[c + 3]), a.c2, -l4.w);
+            float p0 = (c == 12) ? ex2_poly(x0) : ex2(x0);
+            float p1 = (c == 12) ? ex2_poly(x1) : ex2(x1);
+            float p2 = (c == 12) ? ex2_poly(x2) : ex2(x2);
+            float p3 = (c == 12) ? ex2_poly(x3) : ex2(x3);
+            if (lim_hi > 0) {
+              p0 = (cc >= lim) ? p0 : 0.f;
+              p1 = (cc + 1 >= lim) ? p1 : 0.f;
+              p2 = (cc + 2 >= lim) ? p2 : 0.f;
+              p3 = (cc + 3 >= lim) ? p3 : 0.f;
+            }
+            pp[cc >> 1] = pack_bf16(p0, p1);
+            pp[(cc >> 1) + 1] = pack_bf16(p2, p3);
+            dd[cc >> 1] = pack_bf16(p0 * (__uint_as_float(dr[c]) - d4.x), p1 * (__uint_as_float(dr[c + 1]) - d4.y));
+            dd[(cc >> 1) + 1] =
+                pack_bf16(p2 * (__uint_as_float(dr[c + 2]) - d4.z), p3 * (__uint_as_float(dr[c + 3]) - d4.w));
+          }
+        };
+        {
+          uint32_t sr[16], dr[16];
+          tm_ld16(lane_base + cS + uint32_t(32 * g), sr);
+          tm_ld16(lane_base + cdP + uint32_t(32 * g), dr);
+          tm_ld_wait();
+          if (lim_lo <= 31) half(0, sr, dr);
+        }
+        {
+          uint32_t sr[16], dr[16];
+          tm_ld16(lane_base + cS + uint32_t(32 * g + 16), sr);
+          tm_ld16(lane_base + cdP + uint32_t(32 * g + 16), dr);
+          tm_ld_wait();
+          tc_fence_before();
+          mbar_arrive(s_free);
+          if (stamp) dbg_stamp(a, pc, 2);
+          if (lim_lo <= 31) half(16, sr, dr);
+        }
         if (lim_lo > 31) {
 #pragma unroll
           for (int c = 0; c < 16; ++c) { pp[c] = 0u; dd[c] = 0u; }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 32; c += 4) {
-            const float4 l4 = *reinterpret_cast<const float4*>(sLSE + q0 + c);
-            const float4 d4 = *reinterpret_cast<const float4*>(sDel + q0 + c);
-            float p0 = ex2(fmaf(__uint_as_float(sr[c]), a.c2, -l4.x));
-            float p1 = ex2(fmaf(__uint_as_float(sr[c + 1]), a.c2, -l4.y));
-            float p2 = ex2(fmaf(__uint_as_float(sr[c + 2]), a.c2, -l4.z));
-            float p3 = ex2(fmaf(__uint_as_float(sr[c + 3]), a.c2, -l4.w));
-            if (lim_hi > 0) {
-              p0 = (c >= lim) ? p0 : 0.f;
-              p1 = (c + 1 >= lim) ? p1 : 0.f;
-              p2 = (c + 2 >= lim) ? p2 : 0.f;
-              p3 = (c + 3 >= lim) ? p3 : 0.f;
-            }
-            pp[c >> 1] = pack_bf16(p0, p1);
-            pp[(c >> 1) + 1] = pack_bf16(p2, p3);
-            dd[c >> 1] = pack_bf16(p0 * (__uint_as_float(dr[c]) - d4.x), p1 * (__uint_as_float(dr[c + 1]) - d4.y));
-            dd[(c >> 1) + 1] =
-                pack_bf16(p2 * (__uint_as_float(dr[c + 2]) - d4.z), p3 * (__uint_as_float(dr[c + 3]) - d4.w));
-          }
         }
         if (stamp) dbg_stamp(a, pc, 3);
         // the previous pair's products must be done before P / dS are overwritten
+        uint32_t qr[8];
         if (prev_i >= 0) {
           if (!mbar_wait(mma2_done, (pc - 1) & 1, a.err)) { ok = false; break; }
           tc_fence_after();
-          add_dq(prev_i);
-          if (prev_last_kv) write_dkv(b, h, prev_jt);
+          tm_ld8(lane_base + cdQ + uint32_t(8 * g), qr);      // the previous dQ, read while P / dS are stored
         }
-        if (stamp) dbg_stamp(a, pc, 7);
+        if (stamp) dbg_stamp(a, pc, 4);
         // P^T and dS^T into TMEM (A operands of dV / dK), dS^T into the swizzled smem tile (dQ)
         tm_st16(lane_base + cP + uint32_t(16 * g), pp);
         tm_st16(lane_base + cdS + uint32_t(16 * g), dd);
@@ -865,6 +942,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fmha_bwd_tc_kernel(const __gri
             *reinterpret_cast<uint4*>(row + chunk * 16) = make_uint4(dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]);
           }
         }
+        if (prev_i >= 0) {
+          tm_ld_wait8(qr);
+          add_dq(prev_i, qr);
+          if (prev_last_kv) write_dkv(b, h, prev_jt);
+        }
+        if (stamp) dbg_stamp(a, pc, 7);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         tm_st_wait();
         tc_fence_before();
@@ -872,13 +955,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fmha_bwd_tc_kernel(const __gri
         if (stamp) dbg_stamp(a, pc, 13);
         prev_i = it.i;
         prev_jt = it.jt;
-        prev_last_kv = it.last_of_kv();
+        prev_last_kv = it.last_of_kv(a);
       }
       if (!ok) break;
       // ---- item epilogue: the last pair's dQ / dK / dV, then dQ to global ----
       if (!mbar_wait(mma2_done, (pc - 1) & 1, a.err)) { ok = false; break; }
       tc_fence_after();
-      add_dq(prev_i);
+      {
+        uint32_t qr[8];
+        tm_ld8(lane_base + cdQ + uint32_t(8 * g), qr);
+        tm_ld_wait8(qr);
+        add_dq(prev_i, qr);
+      }
       write_dkv(b, h, prev_jt);
       tc_fence_before();
       bar_compute();
@@ -908,7 +996,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fmha_bwd_tc_kernel(const __gri
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
   }
@@ -946,13 +1034,16 @@ void check_qkv5(const at::Tensor& qkv) {
   TORCH_CHECK(reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16 == 0, "qkv must be 16-byte aligned");
 }
 
-// dynamic shared memory of the backward: K, V, Q, dO (two buffers each), the dS
-// tile, lse / delta per query row (padded to whole tiles), the fp32 dQ block, barriers
-size_t bwd_smem_bytes(int q_len) {
+// dynamic shared memory of the backward: K, V (two buffers each), Q, dO (`qst`
+// stages each), the dS tile, lse / delta per query row (padded to whole
+// tiles), the fp32 dQ block, barriers
+size_t bwd_smem_bytes(int q_len, int qst) {
   const int nq = (q_len + atc::kTile - 1) / atc::kTile;
   const int qrows = (q_len + 7) & ~7;
-  return 1024 + 8 * atc::Geo<32>::kTileBytes + 32768 + 2 * size_t(nq) * atc::kTile * 4 + size_t(qrows) * 128 + 256;
+  return 1024 + size_t(4 + 2 * qst) * atc::Geo<32>::kTileBytes + 32768 + 2 * size_t(nq) * atc::kTile * 4 +
+         size_t(qrows) * 128 + 256;
 }
+constexpr size_t kSmemCap = 227 * 1024;
 
 template <int D, int STAGES>
 void launch_fwd(const CUtensorMap& tm, const atc::FwdArgs& a) {
@@ -975,7 +1066,7 @@ void launch_fwd(const CUtensorMap& tm, const atc::FwdArgs& a) {
 // largest q_len whose fp32 dQ block fits the 227 KB of shared memory
 int64_t fmha_bwd_tc_max_q() {
   int q = 64;
-  while (bwd_smem_bytes(q + 64) <= 227 * 1024) q += 64;
+  while (bwd_smem_bytes(q + 8, 2) <= kSmemCap) q += 8;
   return q;
 }
 
@@ -1045,10 +1136,15 @@ void fmha_bwd_tc(at::Tensor qkv, at::Tensor o, at::Tensor lse, at::Tensor dout, 
                                         CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled(dout) failed: ", int(r));
   }
-  const size_t smem = bwd_smem_bytes(int(q_len));
-  PD_CHECK_CUDA(cudaFuncSetAttribute(atc::fmha_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  // three Q / dO stages where the dQ block leaves room for them, else two
   const int grid = a.items < num_sms() ? a.items : num_sms();
-  atc::fmha_bwd_tc_kernel<<<grid, atc::kBwdThreads, smem, stream()>>>(tq, td, a);
+  auto go = [&](auto kern, int qst) {
+    const size_t smem = bwd_smem_bytes(int(q_len), qst);
+    PD_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    kern<<<grid, atc::kBwdThreads, smem, stream()>>>(tq, td, a);
+  };
+  if (bwd_smem_bytes(int(q_len), 3) <= kSmemCap) go(atc::fmha_bwd_tc_kernel<3>, 3);
+  else go(atc::fmha_bwd_tc_kernel<2>, 2);
   PD_CHECK_LAUNCH();
 }
 

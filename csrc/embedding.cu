@@ -392,6 +392,9 @@ struct GradSrc {
   // instead of being applied to the table.
   float* out_rows;
   const int64_t* seg;
+  // When > 0, perm values outside [0, perm_limit) are skipped and recorded as
+  // kIdOutOfRange (the allocation-free entry point takes perm from its caller).
+  int64_t perm_limit;
 };
 
 template <int KV = 8>
@@ -536,6 +539,10 @@ __global__ void __launch_bounds__(256) reduce_update_kernel(
       for (int k = 0; k < 8; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int64_t q = a; q < b; ++q) {
         const int64_t p = src.perm[q];
+        if (src.perm_limit > 0 && uint64_t(p) >= uint64_t(src.perm_limit)) {
+          if (lane == 0) set_error(err, kIdOutOfRange);
+          continue;
+        }
         const int s = find_slot(P.slot_off, P.n_slots, p);
         const Slot& sl = P.slots[s];
         const int64_t i = p - P.slot_off[s];
@@ -1093,6 +1100,15 @@ extern "C" int pd_emb_sparse_update_noalloc(
   if (!sorted_keys || !perm || !grads || !weight || rows <= 0) return PD_NOALLOC_BAD_ARG;
   if ((opt_kind == 1 || opt_kind == 2) && !state1) return PD_NOALLOC_BAD_ARG;
   if (opt_kind == 3 && (!state1 || !state2)) return PD_NOALLOC_BAD_ARG;
+  // The kernel reads a gradient row as 4-element vectors (16 bytes fp32, 8
+  // bytes bf16) and the table / per-element state rows as float4.
+  if (grad_stride < dim || grad_stride % 4 != 0) return PD_NOALLOC_BAD_ARG;
+  auto misaligned = [](const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) != 0; };
+  if (misaligned(grads, grad_dtype == 1 ? 8 : 16) || misaligned(weight, 16)) return PD_NOALLOC_BAD_ARG;
+  if ((opt_kind == 1 || opt_kind == 3) && misaligned(state1, 16)) return PD_NOALLOC_BAD_ARG;
+  if (opt_kind == 2 && misaligned(state1, 4)) return PD_NOALLOC_BAD_ARG;
+  if (opt_kind == 3 && misaligned(state2, 16)) return PD_NOALLOC_BAD_ARG;
+  if (misaligned(sorted_keys, 8) || misaligned(perm, 8) || (err && misaligned(err, 4))) return PD_NOALLOC_BAD_ARG;
 
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -1138,7 +1154,7 @@ extern "C" int pd_emb_sparse_update_noalloc(
   T.n_shards = 1;
   T.dim = dim;
   OptParams O{opt_kind, lr, eps, weight_decay, beta1, beta2, bc1, bc2};
-  GradSrc src{perm, nullptr, nullptr, nullptr, nullptr};
+  GradSrc src{perm, nullptr, nullptr, nullptr, nullptr, n};
   int64_t blocks = (n_chunks + 7) / 8;
   const int64_t cap = int64_t(num_sms()) * 16;
   if (blocks > cap) blocks = cap;

@@ -14,6 +14,8 @@ int64_t fmha_bwd_tc_max_q();
 void tc_gemm(at::Tensor, at::Tensor, at::Tensor, int64_t, c10::optional<at::Tensor>, c10::optional<at::Tensor>,
              at::Tensor, bool);
 void tc_wgrad(at::Tensor, at::Tensor, at::Tensor, at::Tensor, bool);
+at::Tensor tc_mma_rate(int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, at::Tensor);
+at::Tensor tc_mma_burst(int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, at::Tensor);
 }  // namespace pd
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -31,5 +33,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_wgrad", &pd::tc_wgrad, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("err"), py::arg("l_sum") = false,
         "C[l] (fp32, zeroed) += A[l]^T B[l] over rows on tcgen05, split over rows (A [L,K,M], B [L,K,N] bf16 views); "
         "l_sum: one C summed over the batches too");
+  m.def("tc_mma_rate", &pd::tc_mma_rate, py::arg("mode"), py::arg("n"), py::arg("iters"), py::arg("nacc"),
+        py::arg("swz"), py::arg("issue"), py::arg("err"),
+        "tcgen05.mma probe: int64 [SMs, 2] (issue cycles, issue + execution cycles) for `iters` M=128 x n x 16 "
+        "MMAs; mode 0 SS K/K, 1 SS K/MN, 2 SS MN/MN, 3 TS B K-major, 4 TS B MN-major; swz 2 = 128 B, 4 = 64 B; "
+        "issue 0 = lone lane, 1 = converged warp + elect.sync, 2 = as 1 with the lane-mask operand form");
+  m.def("tc_mma_burst", &pd::tc_mma_burst, py::arg("n"), py::arg("iters"), py::arg("issuers"), py::arg("per_sm"),
+        py::arg("ts"), py::arg("wstride"), py::arg("lanes"), py::arg("var"), py::arg("err"),
+        "unrolled tcgen05.mma probe: int64 [CTAs, 8] (issue, total cycles per issuing warp) for iters x 16 MMAs; "
+        "issuers are warps 0, wstride, 2 wstride, ...; var: 0 fixed operands, 1 B advances, 2 A advances, "
+        "3 run-time accumulate flag, 4 not unrolled, 5 = 1 + 2 + 3");
   m.def("launch_count", &pd::launches);
 }

@@ -33,11 +33,18 @@
 // scratch array (cudaGetSymbolAddress) with that device current. Make that
 // first call before any stream capture begins on the device.
 //
+// Alignment: the kernel reads gradient rows as 4-element vectors and table /
+// state rows as float4, so grads must be 16-byte aligned (8 bytes for bf16),
+// weight and the per-element state arrays 16-byte aligned, and grad_stride a
+// multiple of 4 elements with grad_stride >= dim.
+//
 // Return value: 0 on success; PD_NOALLOC_TOO_LARGE if n or dim exceed the
-// limits above; PD_NOALLOC_BAD_ARG for null pointers, dim % 4 != 0 or an
+// limits above; PD_NOALLOC_BAD_ARG for null pointers, dim % 4 != 0, a
+// grad_stride below dim or not a multiple of 4, a misaligned pointer, or an
 // unknown optimizer / dtype; otherwise a cudaError_t value (> 0) from the
-// set-up or the launch. On error nothing is launched. Ids outside
-// [0, rows) are skipped and recorded as 1 in *err (err may be null).
+// set-up or the launch. On error nothing is launched. Table ids outside
+// [0, rows) and perm values outside [0, n) are skipped and recorded as 1 in
+// *err (err may be null; the rest of the call still runs).
 #pragma once
 
 #include <cuda_runtime.h>

@@ -69,9 +69,9 @@ def _tc_fwd_ok(qkv: torch.Tensor) -> bool:
 
 
 # Below this many queries the mma.sync backward is faster on B200 (v6 pyramid,
-# batch 2048: q 283 / kv 409 3.54 vs 3.66 ms, q 158 / kv 283 1.85 vs 2.21 ms,
-# q 32 / kv 158 0.56 vs 1.09 ms; from q 409 up the tcgen05 kernel wins).
-_TC_BWD_MIN_Q = int(os.environ.get("PD_ATTN_TC_BWD_MIN_Q", "300"))
+# batch 2048: q 32 / kv 158 0.56 vs 0.87 ms; q 158 / kv 283 1.86 vs 1.83 ms and
+# every larger layer favour the tcgen05 kernel).
+_TC_BWD_MIN_Q = int(os.environ.get("PD_ATTN_TC_BWD_MIN_Q", "100"))
 
 
 def _tc_bwd_ok(qkv: torch.Tensor, q_len: int) -> bool:
