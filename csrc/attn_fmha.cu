@@ -546,7 +546,7 @@ static void check_qkv(const at::Tensor& t, const char* name) {
 }
 
 // q [B, q_len, H, d] (view), k/v [B, kv_len, H, d] (views) -> (o [B, q_len, H, d], lse [B, H, q_len])
-std::vector<at::Tensor> fmha_fwd(at::Tensor q, at::Tensor k, at::Tensor v, double scale) {
+std::vector<at::Tensor> fmha_fwd(at::Tensor q, at::Tensor k, at::Tensor v, double scale, int64_t warps_req) {
   check_qkv(q, "q"); check_qkv(k, "k"); check_qkv(v, "v");
   const int B = int(q.size(0)), ql = int(q.size(1)), H = int(q.size(2)), D = int(q.size(3));
   const int kl = int(k.size(1));
@@ -561,11 +561,14 @@ std::vector<at::Tensor> fmha_fwd(at::Tensor q, at::Tensor k, at::Tensor v, doubl
                   float(scale * 1.4426950408889634)};
   // d = 32: 64-query CTAs (4 warps, 6 per SM) by default -- v6 pyramid 18.06 ms
   // against 21.38 ms with 128-query CTAs and 18.26 ms with 32-query ones;
-  // PD_FMHA_FWD_WARPS=8 selects the 128-query CTAs.
-  static const int warps = [] {
+  // warps_req = 8 (or, when the caller passes 0, PD_FMHA_FWD_WARPS=8) selects
+  // the 128-query CTAs.
+  TORCH_CHECK(warps_req == 0 || warps_req == 4 || warps_req == 8, "warps: 0 (default), 4 or 8");
+  int warps = int(warps_req);
+  if (warps == 0) {
     const char* e = std::getenv("PD_FMHA_FWD_WARPS");
-    return (e != nullptr && std::atoi(e) == 8) ? 8 : 4;
-  }();
+    warps = (e != nullptr && std::atoi(e) == 8) ? 8 : 4;
+  }
   if (D == 32 && warps == 4) {
     dim3 grid4((ql + 63) / 64, B * H);
     attn::fmha_fwd_kernel<32, 4><<<grid4, 128, 0, stream()>>>(A);

@@ -3,7 +3,7 @@
 #include <torch/extension.h>
 
 namespace pd {
-std::vector<at::Tensor> fmha_fwd(at::Tensor, at::Tensor, at::Tensor, double);
+std::vector<at::Tensor> fmha_fwd(at::Tensor, at::Tensor, at::Tensor, double, int64_t);
 void fmha_bwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor,
               at::Tensor, double);
 long long launches();
@@ -20,7 +20,8 @@ at::Tensor tc_mma_burst(int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, in
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "primus_dlrm_b200 sm_100a tensor-core kernels";
-  m.def("fmha_fwd", &pd::fmha_fwd, "pyramid causal attention forward -> (o, lse)");
+  m.def("fmha_fwd", &pd::fmha_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("scale"), py::arg("warps") = 0,
+        "pyramid causal attention forward -> (o, lse); warps (d = 32): 4 (64-query CTAs), 8 (128), 0 = default");
   m.def("fmha_fwd_tc", &pd::fmha_fwd_tc, "tcgen05 pyramid causal attention forward from qkv [B,T,3,H,d] -> (o, lse)");
   m.def("fmha_bwd_tc", &pd::fmha_bwd_tc, py::arg("qkv"), py::arg("o"), py::arg("lse"), py::arg("dout"),
         py::arg("dqkv"), py::arg("q_len"), py::arg("scale"), py::arg("err"), py::arg("dbg") = py::none(),

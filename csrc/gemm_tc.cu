@@ -758,6 +758,36 @@ namespace {
 // 3-D tensor map over bf16 rows of length K (strides in elements).  mode 0:
 // dims {K, rows, L}; mode 1 (batch stride smaller than the row stride, e.g.
 // one batch per NS token): dims {K, L, rows} so the strides stay ascending.
+// Preconditions of cuTensorMapEncodeTiled checked on the host, so a bad view
+// fails with a message instead of reaching the driver: 16-byte aligned base,
+// extents in [1, 2^32), strides multiples of 16 bytes below 2^40, boxes of
+// 1..256 elements.
+void check_encode(const void* base, const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                  int rank, const char* what) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, what, ": base address not 16-byte aligned");
+  for (int i = 0; i < rank; ++i) {
+    TORCH_CHECK(dims[i] >= 1 && dims[i] < (cuuint64_t(1) << 32), what, ": extent ", i, " out of range (", dims[i], ")");
+    TORCH_CHECK(box[i] >= 1 && box[i] <= 256, what, ": box ", i, " out of range (", box[i], ")");
+  }
+  for (int i = 0; i + 1 < rank; ++i)
+    TORCH_CHECK(strides[i] % 16 == 0 && strides[i] > 0 && strides[i] < (cuuint64_t(1) << 40), what, ": stride ", i,
+                " (", strides[i], " bytes) must be a positive multiple of 16 below 2^40");
+}
+
+// Every element a [L, rows, K] view addresses lies inside its storage (a TMA
+// map of a view reaching past its allocation would read or write memory that
+// is not the tensor's).
+void check_extent(const at::Tensor& t, const char* name) {
+  if (t.numel() == 0) return;
+  int64_t last = t.storage_offset();
+  for (int64_t d = 0; d < t.dim(); ++d) {
+    TORCH_CHECK(t.stride(d) >= 0, name, ": negative strides are not supported");
+    last += (t.size(d) - 1) * t.stride(d);
+  }
+  TORCH_CHECK(int64_t((last + 1) * t.element_size()) <= int64_t(t.storage().nbytes()), name,
+              ": the view reaches past the end of its storage");
+}
+
 CUtensorMap make_map(const void* base, int64_t K, int64_t rows, int64_t L, int64_t row_stride, int64_t l_stride,
                      int box_rows, int& mode) {
   CUtensorMap m;
@@ -775,6 +805,7 @@ CUtensorMap make_map(const void* base, int64_t K, int64_t rows, int64_t L, int64
     box[0] = tc::BK; box[1] = 1; box[2] = box_rows;
   }
   cuuint32_t estr[3] = {1, 1, 1};
+  check_encode(base, dims, strides, box, 3, "operand map");
   CUresult r = tensor_map_encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
                                       box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -803,6 +834,7 @@ CUtensorMap make_store_map(const void* base, int64_t N, int64_t rows, int64_t L,
     box[0] = 32; box[1] = 1; box[2] = 32;
   }
   cuuint32_t estr[3] = {1, 1, 1};
+  check_encode(base, dims, strides, box, 3, "epilogue map");
   CUresult r = tensor_map_encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
                                       box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                                       CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -818,6 +850,7 @@ void check_operand(const at::Tensor& t, const char* name) {
   TORCH_CHECK(t.stride(1) % 8 == 0 && (t.size(0) == 1 || t.stride(0) % 8 == 0) &&
               reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, ": rows must be 16-byte aligned");
   TORCH_CHECK(t.size(2) % 8 == 0, name, ": K must be a multiple of 8");
+  check_extent(t, name);
 }
 
 template <int BN, int STAGES>
@@ -853,6 +886,9 @@ void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optiona
   TORCH_CHECK(C.dim() == 3 && C.size(0) == L && C.size(1) == M && C.size(2) == N && C.stride(2) == 1 &&
               C.scalar_type() == at::kBFloat16 && C.stride(1) % 8 == 0 && (C.size(0) == 1 || C.stride(0) % 8 == 0) &&
               reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0, "C must be a [L, M, N] bf16 view with aligned rows");
+  check_extent(C, "C");
+  if (R && R->defined()) check_extent(*R, "R");
+  if (AUX && AUX->defined()) check_extent(*AUX, "AUX");
   tc::Params p{};
   p.M = int(M); p.N = int(N); p.K = int(K); p.L = int(L);
   p.m_blocks = int((M + tc::BM - 1) / tc::BM);

@@ -91,6 +91,9 @@ def _err_word(device) -> torch.Tensor:
 
 
 _ERR: dict = {}
+# calls of the native attention kernels (forward, backward) since import: a
+# check that a run took the kernel path and not the PyTorch fallback
+NATIVE_CALLS = {"fwd": 0, "bwd": 0}
 
 
 def attention_error_code(device) -> int:
@@ -113,6 +116,7 @@ class _NativeFMHAFused(torch.autograd.Function):
             o, lse = G.fmha_fwd_tc(qkv, q_len, scale, _err_word(qkv.device))
         else:
             o, lse = G.fmha_fwd(q, k, v, scale)
+        NATIVE_CALLS["fwd"] += 1
         ctx.scale, ctx.q_len = scale, q_len
         ctx.save_for_backward(qkv, o, lse)
         return o
@@ -123,6 +127,7 @@ class _NativeFMHAFused(torch.autograd.Function):
         qkv, o, lse = ctx.saved_tensors
         T, ql = qkv.shape[1], ctx.q_len
         dqkv = torch.empty_like(qkv)
+        NATIVE_CALLS["bwd"] += 1
         if _tc_bwd_ok(qkv, ql):
             G.fmha_bwd_tc(qkv, o, lse, do.contiguous(), dqkv, ql, ctx.scale, _err_word(qkv.device))
             return dqkv, None, None

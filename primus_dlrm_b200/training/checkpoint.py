@@ -85,6 +85,14 @@ def load_checkpoint(path: str | Path, model, engine=None, strict: bool = True) -
             engine.sparse_opt.step = int(ckpt["sparse_optimizer_step"])
     if "rng_state" in ckpt:
         torch.set_rng_state(ckpt["rng_state"]["cpu"])
+        # the CUDA generator of this process's device (dropout, on-device
+        # sampling); only the current device is touched, so no other GPU gets
+        # a context
+        cuda_states = ckpt["rng_state"].get("cuda") or []
+        if torch.cuda.is_available() and cuda_states:
+            dev = torch.cuda.current_device()
+            if dev < len(cuda_states):
+                torch.cuda.set_rng_state(cuda_states[dev], device=dev)
     return ckpt
 
 

@@ -27,6 +27,7 @@ from primus_dlrm_b200.config import Config
 from primus_dlrm_b200.data.batch import PackedBatch
 from primus_dlrm_b200.ops.optim import FlatParams, FusedAdamW
 from primus_dlrm_b200.training.losses import InBatchBPRLoss, MultiTaskLoss
+from primus_dlrm_b200.utils.nvtx import phase
 
 
 def dense_parameters(model: nn.Module) -> list[nn.Parameter]:
@@ -98,26 +99,29 @@ class TrainEngine:
             self.sparse_opt.lr_scale = tc.sparse_warmup_value if self.global_step < tc.sparse_warmup_steps else 1.0
         self.model.train()
         self.flat.zero_grad()
-        with torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.use_amp):
+        with phase("pd.forward"), torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.use_amp):
             total, task_losses = self.compute_loss(batch)
         ex = self._overlap_executor()
         if ex is not None:
             # the dense all-reduce starts when the lookup's backward begins (every
             # dense gradient is final by then) and runs beside the sparse exchange
             ex.pre_backward = lambda: self.grad_sync.start_async(self.flat.grad)
-        total.backward()
+        with phase("pd.backward"):
+            total.backward()
         if ex is not None:
             ex.pre_backward = None
         if self.grad_sync is not None:
-            if not (ex is not None and self.grad_sync.finish_async()):
-                self.grad_sync.sync(self.flat.grad)
-        if tc.nan_guard and not bool(torch.isfinite(total)):
-            self.skipped_steps += 1
-        elif getattr(self.grad_sync, "sharded", False) and isinstance(self.optimizer, FusedAdamW):
-            self.optimizer.step(shard=self.grad_sync.shard_range(self.flat.numel), group=self.grad_sync.group)
-            self.grad_sync.gather_params(self.flat.data)
-        else:
-            self.optimizer.step()
+            with phase("pd.dense_sync"):
+                if not (ex is not None and self.grad_sync.finish_async()):
+                    self.grad_sync.sync(self.flat.grad)
+        with phase("pd.optimizer"):
+            if tc.nan_guard and not bool(torch.isfinite(total)):
+                self.skipped_steps += 1
+            elif getattr(self.grad_sync, "sharded", False) and isinstance(self.optimizer, FusedAdamW):
+                self.optimizer.step(shard=self.grad_sync.shard_range(self.flat.numel), group=self.grad_sync.group)
+                self.grad_sync.gather_params(self.flat.data)
+            else:
+                self.optimizer.step()
         self.scheduler.step()
         self.global_step += 1
         return total.detach(), task_losses

@@ -2,8 +2,10 @@
 
 For every requested step ``s`` the schedule records ``[s - warmup, s)`` as
 warm-up and ``[s, s + active)`` as active, saving one Chrome trace per
-window as ``trace_step{s}[_rank{r}].json``.  Native kernels carry NVTX ranges
-(``primus_dlrm_b200.utils.nvtx``) so trace tools can classify them.
+window as ``trace_step{s}[_rank{r}].json``.  The step's phases carry NVTX
+ranges and profiler labels (``pd.forward``, ``pd.backward``, ``pd.dense_sync``,
+``pd.optimizer``; ``primus_dlrm_b200.utils.nvtx``) so trace tools can
+attribute kernels to them.
 """
 from __future__ import annotations
 

@@ -10,7 +10,6 @@ source is compiled for ``sm_100a`` only.
 from __future__ import annotations
 
 import glob
-import importlib.util
 import os
 
 from setuptools import setup
@@ -18,17 +17,6 @@ from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-
-
-def cutlass_include() -> list[str]:
-    """CUTLASS/CuTe header tree vendored with flashinfer (sm100 collectives)."""
-    spec = importlib.util.find_spec("flashinfer")
-    cands = []
-    if spec is not None and spec.submodule_search_locations:
-        for loc in spec.submodule_search_locations:
-            cands.append(os.path.join(loc, "data", "cutlass", "include"))
-            cands.append(os.path.join(loc, "data", "cutlass", "tools", "util", "include"))
-    return [c for c in cands if os.path.isdir(c)]
 
 
 NVCC_COMMON = ARCH + [
@@ -56,10 +44,10 @@ if os.path.exists(os.path.join(ROOT, "csrc", "gemm_bindings.cpp")):
     ext_modules.append(CUDAExtension(
         name="primus_dlrm_b200._gemm",
         sources=gemm_sources,
-        include_dirs=[os.path.join(ROOT, "csrc")] + cutlass_include(),
+        include_dirs=[os.path.join(ROOT, "csrc")],
         extra_compile_args={
             "cxx": CXX,
-            "nvcc": NVCC_COMMON + ["-DCUTLASS_ENABLE_TENSOR_CORE_MMA=1", "--use_fast_math",
+            "nvcc": NVCC_COMMON + ["--use_fast_math",
                                    "-Xptxas=-v" if os.environ.get("PD_PTXAS_V") else "-DPD_NOV"],
         },
     ))

@@ -129,3 +129,18 @@ def test_fmha_tc_bwd_matches_reference(ql, kl):
         sc = x.grad[:, :, part].abs().max().item() + 1e-6
         assert e / sc < 3e-2, f"part {part}: max err {e} (scale {sc})"
     assert torch.all(g[:, : kl - ql, 0] == 0)
+
+
+@pytest.mark.parametrize("warps", [4, 8])
+@pytest.mark.parametrize("ql,kl", [(912, 912), (158, 283), (1, 70), (130, 257)])
+def test_fmha_fwd_cta_sizes_match_reference(warps, ql, kl):
+    """Both CTA sizes of the mma.sync forward (64- and 128-query CTAs, d = 32)."""
+    from primus_dlrm_b200.ops import _ext
+    G = _ext.gemm()
+    torch.manual_seed(ql + kl + warps)
+    B, H, d = 2, 4, 32
+    qkv = torch.randn(B, kl, 3, H, d, device="cuda").to(torch.bfloat16)
+    q, k, v = qkv[:, kl - ql:, 0], qkv[:, :, 1], qkv[:, :, 2]
+    o, lse = G.fmha_fwd(q, k, v, d ** -0.5, warps)
+    x = qkv.float()
+    torch.testing.assert_close(o.float(), _ref(x[:, kl - ql:, 0], x[:, :, 1], x[:, :, 2]), rtol=2e-2, atol=2e-2)
