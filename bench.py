@@ -149,6 +149,12 @@ def main() -> None:
 
     cfg = Config.load(args.config)
     cfg.train.batch_size = args.per_gpu_batch * world
+    model_desc = MODEL_DESC
+    if os.path.abspath(args.config) != os.path.abspath(CONFIG):
+        ot = cfg.model.transformer
+        model_desc = (f"{os.path.splitext(os.path.basename(args.config))[0]}: {ot.n_layers}L d{ot.d_model} "
+                      f"{ot.n_heads}hx{ot.d_model // ot.n_heads} NS{ot.n_ns_tokens} L_S{cfg.sequence_length_total()} "
+                      f"E{cfg.model.embedding_dim}")
     if args.impl == "eager":
         cfg.train.kernels = "eager"
     if args.comm:
@@ -193,7 +199,9 @@ def main() -> None:
     if world > 1:
         dist.barrier()
     launches = (C.launch_count() - l0) if C is not None else 0
-    if gemm is not None and hasattr(gemm, "launch_count"):
+    # the two extensions may share one counter (the dynamic linker merges the
+    # header's counter when both are loaded); add the second only if distinct
+    if gemm is not None and hasattr(gemm, "launch_count") and g0 != l0:
         launches += gemm.launch_count() - g0
     ms = ev0.elapsed_time(ev1) / args.steps
     a2a_ms = engine.exposed_comm_ms() / args.steps
@@ -235,9 +243,9 @@ def main() -> None:
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded Zipf ids, random-init weights)",
             "impl": args.impl,
-            "config": {"model": MODEL_DESC, "global_batch": gb, "seq_len": cfg.sequence_length_total() + 16,
+            "config": {"model": model_desc, "global_batch": gb, "seq_len": cfg.sequence_length_total() + 16,
                        "parallelism": f"dp{world}" + (" + row-wise sharded tables" if world > 1 else ""),
-                       "l2": "no flush: inputs exceed L2 (7.7 GB tables, >10 GB activations per step)",
+                       "l2": "no flush: inputs exceed L2 (GB-scale tables, >10 GB activations per step)",
                        "embedding_optimizer": cfg.train.embedding_optimizer},
             "e2e": {"value": round(gb / (e2e_ms / 1000.0), 1), "unit": "samples/s",
                     "h2d_bytes_per_step": packed[0].nbytes, "d2h_bytes_per_step": 4,
