@@ -5,22 +5,11 @@
 // the LAST q_len of the T tokens of a [B, T, 3, H, d] fused projection; query
 // i (absolute position p = T - q_len + i) attends keys j <= p; scale 1/sqrt(d).
 //
-// Forward, one CTA = one 128-query tile at a time (persistent over tiles, two
-// CTAs per SM so one CTA's softmax overlaps the other's matrix work):
-//   warp 0     TMA: the Q tile (double-buffered across items), then K_j / V_j
-//              tiles into a ring
-//   warp 1     TMEM owner + MMA issuer (one elected lane):
-//                S_j  = Q K_j^T            (SS: both operands in smem, K-major)
-//                O   += P_{j-1} V_{j-1}    (TS: P from TMEM, V in smem MN-major)
-//   warps 2-5  softmax: thread = query row = TMEM lane, so row max / sum need
-//              no shuffles; the 128-key row is read from TMEM twice (max,
-//              then exp) in 64-column halves. The running max is only raised
-//              when it grows by more than 2^8 (log2 domain), so O in TMEM is
-//              rescaled rarely.
-//              P (bf16) goes back to TMEM for the PV product; l and O use the
-//              same reference max, so a stale max is exact.
-// TMEM (256 columns): S [0,128) fp32, O [128, 128+d) fp32, P [128+d, 128+2d)
-// as packed bf16 pairs (64 columns for a 128-key row).
+// Forward (fmha_fwd_tc_kernel): 128-query tiles, 64-key S tiles triple-
+// buffered in TMEM with P written back over them, S issued two tiles ahead of
+// the softmax; details at the kernel. Backward (fmha_bwd_tc_kernel, d = 32):
+// one CTA per (b, h), one MMA-issuing warp per product stream; details at
+// the kernel.
 //
 // Every wait is bounded (2 s on %globaltimer); on timeout the error word
 // gets kWaitTimeout, the roles leave their loops, drain their own in-flight
@@ -163,19 +152,40 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x on the FMA/ALU pipes, used for a quarter of the exponentials so the
-// MUFU unit (16 ex2 per clock per SM) is not the only one working: Cody-Waite
-// style reduction x = n + f with n = round(x) via the 1.5 * 2^23 shifter and
-// f in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients were
-// fitted here (iteratively reweighted least squares on Chebyshev nodes,
-// max relative error 7.5e-5, well below the bf16 rounding of P); 2^n is
-// added to the exponent field. Inputs below -125 return ~2^-125.
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -125.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  const float p = fmaf(fmaf(fmaf(0.055179596f, f, 0.24261186f), f, 0.69325954f), f, 0.99992800f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes'
+// worth of FMA / add) and the three-input max.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma_f2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_f2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t sub_f2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul_f2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -223,40 +233,83 @@ struct FwdArgs {
 };
 
 constexpr int kFwdThreads = 192;
+constexpr int kKT = 64;                  // keys per S tile
+constexpr int kSBuf = 3;                 // S / P buffers in TMEM
 
-template <int D, int STAGES>
-__global__ void __launch_bounds__(kFwdThreads, 2) fmha_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm,
+// Tile enumeration shared by the roles: this CTA's items (b, h, 128-query
+// tile), then the 64-key tiles the query tile sees.
+struct FwdIt {
+  int w, j, nkv, i0, b, h;
+  __device__ void load(const FwdArgs& a) {
+    const int bh = w / a.nq;
+    i0 = (w - bh * a.nq) * kTile;
+    b = bh / a.H;
+    h = bh - b * a.H;
+    const int last = min(a.T - 1, a.T - a.q_len + i0 + kTile - 1);
+    nkv = last / kKT + 1;
+  }
+  __device__ void start(const FwdArgs& a, int wb, int we) { w = wb; j = 0; if (w < we) load(a); }
+  __device__ bool last_of_item() const { return j == nkv - 1; }
+  __device__ void next(const FwdArgs& a, int we) {
+    if (++j < nkv) return;
+    ++w; j = 0;
+    if (w < we) load(a);
+  }
+};
+
+// Forward: one CTA = one 128-query tile at a time (persistent over this CTA's
+// contiguous item range), two CTAs per SM.
+//   warp 0     TMA: the Q tile (double-buffered across items), 64-key K / V
+//              tiles into a KST-deep ring
+//   warp 1     TMEM owner + MMA issuer: S_t = Q K_t^T (SS) two tiles ahead of
+//              the softmax, O += P_t V_t (TS: P from TMEM) as each P is ready
+//   warps 2-5  softmax: thread = query row = TMEM lane; the 64-key S row is
+//              read from TMEM once, its max and exponentials computed in
+//              registers, and P (bf16 pairs) written back over the S columns
+// TMEM (256 columns): S / P buffers [64 b, 64 b + 64) for b < 3 (P in the
+// first 32 columns of its S tile), O [192, 192 + d).
+// S of tile t goes to buffer t % 3; it is issued after PV(t - 2), once PV(t - 3)
+// (the last reader of that buffer's P) completed. The running max is raised
+// only when it grows by more than 2^8 (log2 domain), so O is rescaled rarely;
+// a rescale first waits for the PV product of the previous tile.
+template <int D, int KST>
+__global__ void __launch_bounds__(kFwdThreads, 2) fmha_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+                                                                     const __grid_constant__ CUtensorMap tm_kv,
                                                                      const FwdArgs a) {
   using G = Geo<D>;
   constexpr uint32_t kCols = 256;
-  constexpr uint32_t cS = 0, cO = 128, cP = 128 + D;
+  constexpr uint32_t cO = kSBuf * kKT;
+  constexpr int kQBytes = kTile * G::RB;
+  constexpr int kKVBytes = kKT * G::RB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                                   // two Q buffers (next item's Q prefetched)
-  uint8_t* sK = sQ + 2 * G::kTileBytes;
-  uint8_t* sV = sK + STAGES * G::kTileBytes;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sV + STAGES * G::kTileBytes);
-  uint64_t* q_full = bar;       // [2]
-  uint64_t* q_empty = bar + 2;  // [2]
-  uint64_t* s_full = bar + 4;
-  uint64_t* p_full = bar + 5;
-  uint64_t* o_full = bar + 6;
-  uint64_t* o_free = bar + 7;
-  uint64_t* mma_done = bar + 8;
-  uint64_t* kv_full = bar + 9;
-  uint64_t* kv_empty = kv_full + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kv_empty + STAGES);
+  uint8_t* sQ = smem;                                 // [2] Q tiles (next item's Q prefetched)
+  uint8_t* sK = sQ + 2 * kQBytes;                     // [KST]
+  uint8_t* sV = sK + KST * kKVBytes;                  // [KST]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sV + KST * kKVBytes);
+  uint64_t* q_full = bar;                 // [2]
+  uint64_t* q_empty = bar + 2;            // [2]
+  uint64_t* kv_full = bar + 4;            // [KST]
+  uint64_t* kv_empty = kv_full + KST;     // [KST]
+  uint64_t* s_full = kv_empty + KST;      // [3]
+  uint64_t* p_full = s_full + kSBuf;      // [3]
+  uint64_t* pv_done = p_full + kSBuf;     // [3]
+  uint64_t* o_full = pv_done + kSBuf;
+  uint64_t* o_free = o_full + 1;
+  uint64_t* mma_done = o_free + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    mbar_init(&q_full[0], 1); mbar_init(&q_full[1], 1); mbar_init(&q_empty[0], 1); mbar_init(&q_empty[1], 1);
-    mbar_init(s_full, 1); mbar_init(p_full, 128);
+    for (int k = 0; k < 2; ++k) { mbar_init(&q_full[k], 1); mbar_init(&q_empty[k], 1); }
+    for (int k = 0; k < KST; ++k) { mbar_init(&kv_full[k], 1); mbar_init(&kv_empty[k], 1); }
+    for (int k = 0; k < kSBuf; ++k) { mbar_init(&s_full[k], 1); mbar_init(&p_full[k], 128); mbar_init(&pv_done[k], 1); }
     mbar_init(o_full, 1); mbar_init(o_free, 128); mbar_init(mma_done, 1);
-    for (int s = 0; s < STAGES; ++s) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&tm) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_q) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_kv) : "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -274,95 +327,94 @@ __global__ void __launch_bounds__(kFwdThreads, 2) fmha_fwd_tc_kernel(const __gri
   const int w_begin = blockIdx.x * per;
   const int w_end = min(a.items, w_begin + per);
 
-  auto decode = [&](int w, int& b, int& h, int& i0, int& nkv) {
-    const int bh = w / a.nq;
-    i0 = (w - bh * a.nq) * kTile;
-    b = bh / a.H;
-    h = bh - b * a.H;
-    const int last = min(a.T - 1, off + i0 + kTile - 1);
-    nkv = last / kTile + 1;
-  };
-
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      int kv_cnt = 0, item = 0;
-      int issued_q[2] = {0, 0}, issued_kv[STAGES];
+      FwdIt it;
+      it.start(a, w_begin, w_end);
+      int item = 0, kvc = 0;
+      int issued_q[2] = {0, 0}, issued_kv[KST];
 #pragma unroll
-      for (int s = 0; s < STAGES; ++s) issued_kv[s] = 0;
-      for (int w = w_begin; w < w_end && !*abort_flag; ++w, ++item) {
-        int b, h, i0, nkv;
-        decode(w, b, h, i0, nkv);
-        const int qb = item & 1;
-        if (!mbar_wait(&q_empty[qb], ((item >> 1) & 1) ^ 1, a.err)) { *abort_flag = 1; break; }
-        mbar_expect_tx(&q_full[qb], G::kTileBytes);
-        tma_load_5d(sQ + qb * G::kTileBytes, &tm, &q_full[qb], 0, h, 0, off + i0, b);
-        ++issued_q[qb];
-        for (int j = 0; j < nkv; ++j, ++kv_cnt) {
-          const int st = kv_cnt % STAGES, n = kv_cnt / STAGES;
-          if (!mbar_wait(&kv_empty[st], (n & 1) ^ 1, a.err)) { *abort_flag = 1; break; }
-          mbar_expect_tx(&kv_full[st], 2 * G::kTileBytes);
-          tma_load_5d(sK + st * G::kTileBytes, &tm, &kv_full[st], 0, h, 1, j * kTile, b);
-          tma_load_5d(sV + st * G::kTileBytes, &tm, &kv_full[st], 0, h, 2, j * kTile, b);
-          ++issued_kv[st];
+      for (int k = 0; k < KST; ++k) issued_kv[k] = 0;
+      bool good = true;
+      while (good && it.w < w_end && !*abort_flag) {
+        if (it.j == 0) {
+          const int qb = item & 1;
+          if (!mbar_wait(&q_empty[qb], ((item >> 1) & 1) ^ 1, a.err)) { good = false; break; }
+          mbar_expect_tx(&q_full[qb], kQBytes);
+          tma_load_5d(sQ + qb * kQBytes, &tm_q, &q_full[qb], 0, it.h, 0, off + it.i0, it.b);
+          ++issued_q[qb];
         }
+        const int st = kvc % KST;
+        if (!mbar_wait(&kv_empty[st], ((kvc / KST) & 1) ^ 1, a.err)) { good = false; break; }
+        mbar_expect_tx(&kv_full[st], 2 * kKVBytes);
+        tma_load_5d(sK + st * kKVBytes, &tm_kv, &kv_full[st], 0, it.h, 1, it.j * kKT, it.b);
+        tma_load_5d(sV + st * kKVBytes, &tm_kv, &kv_full[st], 0, it.h, 2, it.j * kKT, it.b);
+        ++issued_kv[st];
+        ++kvc;
+        if (it.last_of_item()) ++item;
+        it.next(a, w_end);
       }
+      if (!good) *abort_flag = 1;
       if (*abort_flag) {  // every issued copy lands before the CTA may exit
         for (int qb = 0; qb < 2; ++qb)
           if (issued_q[qb] > 0) (void)mbar_wait(&q_full[qb], uint32_t(issued_q[qb] - 1) & 1u, a.err);
 #pragma unroll
-        for (int s = 0; s < STAGES; ++s)
-          if (issued_kv[s] > 0) (void)mbar_wait(&kv_full[s], uint32_t(issued_kv[s] - 1) & 1u, a.err);
+        for (int s2 = 0; s2 < KST; ++s2)
+          if (issued_kv[s2] > 0) (void)mbar_wait(&kv_full[s2], uint32_t(issued_kv[s2] - 1) & 1u, a.err);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t id_s = idesc(128, 128, 0, 0);
+      constexpr uint32_t id_s = idesc(128, kKT, 0, 0);
       constexpr uint32_t id_pv = idesc(128, D, 0, 1);
-      int kv_cnt = 0, tile = 0, item = 0;
-      for (int w = w_begin; w < w_end && !*abort_flag; ++w, ++item) {
-        int b, h, i0, nkv;
-        decode(w, b, h, i0, nkv);
-        const int qb = item & 1;
-        if (!mbar_wait(&q_full[qb], (item >> 1) & 1, a.err)) { *abort_flag = 1; break; }
+      FwdIt si, pi;
+      si.start(a, w_begin, w_end);
+      pi.start(a, w_begin, w_end);
+      int ts = 0, tp = 0, s_item = 0, p_item = 0;
+      bool good = true;
+      auto issue_s = [&]() {
+        const int qb = s_item & 1;
+        if (si.j == 0 && !mbar_wait(&q_full[qb], (s_item >> 1) & 1, a.err)) return false;
+        const int st = ts % KST, buf = ts % kSBuf;
+        if (!mbar_wait(&kv_full[st], (ts / KST) & 1, a.err)) return false;
+        if (ts >= kSBuf && !mbar_wait(&pv_done[buf], uint32_t(ts / kSBuf - 1) & 1u, a.err)) return false;
         tc_fence_after();
-        int prev_st = 0;
-        bool ok = true;
-        for (int j = 0; j <= nkv; ++j) {
-          int st = 0;
-          if (j < nkv) {
-            st = kv_cnt % STAGES;
-            if (!mbar_wait(&kv_full[st], (kv_cnt / STAGES) & 1, a.err)) { ok = false; break; }
-            tc_fence_after();
-          }
-          if (j > 0) {
-            // O += P_{j-1} V_{j-1}
-            if (!mbar_wait(p_full, (tile - 1) & 1, a.err)) { ok = false; break; }
-            if (j == 1 && !mbar_wait(o_free, (item & 1) ^ 1, a.err)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t vt = smem_u32(sV + prev_st * G::kTileBytes);
+        const uint32_t qt = smem_u32(sQ + qb * kQBytes), kt = smem_u32(sK + st * kKVBytes);
 #pragma unroll
-            for (int kk = 0; kk < kTile / 16; ++kk)
-              mma_ts(tmem + cO, tmem + cP + uint32_t(kk * 8), desc_mn<D>(vt, kk), id_pv, (j > 1 || kk > 0) ? 1u : 0u);
-            tc_commit(&kv_empty[prev_st]);
-          }
-          if (j < nkv) {
-            // S_j = Q K_j^T
-            const uint32_t qt = smem_u32(sQ + qb * G::kTileBytes), kt = smem_u32(sK + st * G::kTileBytes);
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(tmem + uint32_t(kKT * buf), desc_k<D>(qt, kk), desc_k<D>(kt, kk), id_s, kk > 0 ? 1u : 0u);
+        tc_commit(&s_full[buf]);
+        if (si.last_of_item()) { tc_commit(&q_empty[qb]); ++s_item; }
+        si.next(a, w_end);
+        ++ts;
+        return true;
+      };
+      auto issue_pv = [&]() {
+        const int st = tp % KST, buf = tp % kSBuf;
+        if (!mbar_wait(&p_full[buf], uint32_t(tp / kSBuf) & 1u, a.err)) return false;
+        if (pi.j == 0 && !mbar_wait(o_free, (p_item & 1) ^ 1, a.err)) return false;
+        tc_fence_after();
+        const uint32_t vt = smem_u32(sV + st * kKVBytes);
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk)
-              mma_ss(tmem + cS, desc_k<D>(qt, kk), desc_k<D>(kt, kk), id_s, kk > 0 ? 1u : 0u);
-            tc_commit(s_full);
-            if (j == nkv - 1) tc_commit(&q_empty[qb]);
-            prev_st = st;
-            ++kv_cnt;
-            ++tile;
-          }
-        }
-        if (!ok) { *abort_flag = 1; break; }
-        tc_commit(o_full);
+        for (int kk = 0; kk < kKT / 16; ++kk)
+          mma_ts(tmem + cO, tmem + uint32_t(kKT * buf + 8 * kk), desc_mn<D>(vt, kk), id_pv,
+                 (pi.j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&kv_empty[st]);
+        tc_commit(&pv_done[buf]);
+        if (pi.last_of_item()) { tc_commit(o_full); ++p_item; }
+        pi.next(a, w_end);
+        ++tp;
+        return true;
+      };
+      // S runs two tiles ahead of PV
+      for (int k = 0; k < 2 && good && si.w < w_end; ++k) good = issue_s();
+      while (good && pi.w < w_end && !*abort_flag) {
+        good = issue_pv();
+        if (good && si.w < w_end) good = issue_s();
       }
+      if (!good) *abort_flag = 1;
       tc_commit(mma_done);
       (void)mbar_wait(mma_done, 0, a.err);
     }
@@ -371,43 +423,44 @@ __global__ void __launch_bounds__(kFwdThreads, 2) fmha_fwd_tc_kernel(const __gri
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;                      // row of the tile = TMEM lane
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
-    int tile = 0, item = 0;
-    for (int w = w_begin; w < w_end && !*abort_flag; ++w, ++item) {
-      int b, h, i0, nkv;
-      decode(w, b, h, i0, nkv);
-      const int p_abs = off + i0 + r;                       // this row's last visible key
+    FwdIt it;
+    it.start(a, w_begin, w_end);
+    int t = 0, item = 0;
+    bool ok = true;
+    while (ok && it.w < w_end && !*abort_flag) {
+      const int p_abs = off + it.i0 + r;                    // this row's last visible key
       float m = -1e30f, l = 0.f;
-      bool ok = true;
-      for (int j = 0; j < nkv; ++j, ++tile) {
-        if (!mbar_wait(s_full, tile & 1, a.err)) { ok = false; break; }
+      const int b = it.b, h = it.h, i0 = it.i0;
+      for (;;) {
+        const int buf = t % kSBuf, j = it.j;
+        if (!mbar_wait(&s_full[buf], uint32_t(t / kSBuf) & 1u, a.err)) { ok = false; break; }
         tc_fence_after();
-        const int lim = p_abs - j * kTile;                  // keys c <= lim are visible
-        const bool diag = __any_sync(0xffffffffu, lim < kTile - 1);   // warp-uniform masking
-        // pass 1: row max (8 independent partial maxima)
-        float mx8[8];
+        uint32_t sr[64];
+        tm_ld32(lane_base + uint32_t(kKT * buf), sr);
+        tm_ld32(lane_base + uint32_t(kKT * buf + 32), sr + 32);
+        tm_ld_wait();
+        const int lim = p_abs - j * kKT;                    // keys c <= lim are visible
+        const bool diag = __any_sync(0xffffffffu, lim < kKT - 1);   // warp-uniform masking
+        if (diag) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
-#pragma unroll
-        for (int h0 = 0; h0 < kTile; h0 += 64) {
-          uint32_t sr[64];
-          tm_ld32(lane_base + cS + h0, sr);
-          tm_ld32(lane_base + cS + h0 + 32, sr + 32);
-          tm_ld_wait();
-          if (diag) {
-#pragma unroll
-            for (int c = 0; c < 64; ++c)
-              mx8[c & 7] = fmaxf(mx8[c & 7], (h0 + c <= lim) ? __uint_as_float(sr[c]) : -INFINITY);
-          } else {
-#pragma unroll
-            for (int c = 0; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sr[c]));
-          }
+          for (int c = 0; c < 64; ++c) sr[c] = (c <= lim) ? sr[c] : __float_as_uint(-INFINITY);
         }
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        // row max: four chains of three-input maxima
+        float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+          mxa = max3(mxa, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+          mxb = max3(mxb, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+          mxc = max3(mxc, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+          mxd = max3(mxd, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+        }
+        const float mx = fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd));
         const float m_new = fmaxf(m, mx * a.c2);
         const bool need = m_new > m + 8.0f;
         if (__any_sync(0xffffffffu, need && j > 0)) {
-          // rescale O (quiescent: every earlier PV product completed before S_j)
+          // rescale O once the previous tile's PV product (the last writer) completed
+          if (!mbar_wait(&pv_done[(t - 1) % kSBuf], uint32_t((t - 1) / kSBuf) & 1u, a.err)) { ok = false; break; }
+          tc_fence_after();
           const float alpha = need ? ex2(m - m_new) : 1.f;
 #pragma unroll
           for (int c0 = 0; c0 < D; c0 += 32) {
@@ -418,48 +471,50 @@ __global__ void __launch_bounds__(kFwdThreads, 2) fmha_fwd_tc_kernel(const __gri
             for (int c = 0; c < 32; ++c) orr[c] = __float_as_uint(__uint_as_float(orr[c]) * alpha);
             tm_st32(lane_base + cO + c0, orr);
           }
+          tm_st_wait();
         }
         if (need) {
           l *= ex2(m - m_new);
           m = m_new;
         }
-        // pass 2: P = exp2(S c - m) -> bf16 pairs in TMEM (8 independent partial sums)
-        float sm8[8];
+        // P = exp2(S c - m) -> bf16 pairs over the S columns, with S c - m and
+        // the row sums as packed pairs. All exponentials on the MUFU unit: this
+        // loop is bound by instruction issue and latency, so moving some of
+        // them to an FMA-pipe polynomial measured slower (v6 layer 0: 4.43 ms
+        // with none, slower with 8, 16 or 24 of the 64 columns moved).
+        // Masked columns hold -inf: ex2 -> 0.
+        const uint64_t c2v = f2(a.c2, a.c2), nmv = f2(-m, -m);
+        uint64_t acc0 = f2(0.f, 0.f), acc1 = acc0, acc2 = acc0, acc3 = acc0;
+        uint32_t pk[32];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) sm8[e] = 0.f;
-#pragma unroll
-        for (int h0 = 0; h0 < kTile; h0 += 64) {
-          uint32_t sr[64];
-          tm_ld32(lane_base + cS + h0, sr);
-          tm_ld32(lane_base + cS + h0 + 32, sr + 32);
-          tm_ld_wait();
-#pragma unroll
-          for (int q0 = 0; q0 < 64; q0 += 32) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int c = 0; c < 32; c += 2) {
-              const int k0 = h0 + q0 + c;
-              const float x0 = fmaf(__uint_as_float(sr[q0 + c]), a.c2, -m);
-              const float x1 = fmaf(__uint_as_float(sr[q0 + c + 1]), a.c2, -m);
-              float p0 = (c >= 24) ? ex2_poly(x0) : ex2(x0);   // columns 24..31 of each 32 on the FMA pipe
-              float p1 = (c >= 24) ? ex2_poly(x1) : ex2(x1);
-              if (diag) {
-                p0 = (k0 <= lim) ? p0 : 0.f;
-                p1 = (k0 + 1 <= lim) ? p1 : 0.f;
-              }
-              sm8[(c >> 1) & 7] += p0 + p1;
-              pk[c >> 1] = pack_bf16(p0, p1);
-            }
-            tm_st16(lane_base + cP + uint32_t((h0 + q0) >> 1), pk);
+        for (int c = 0; c < 64; c += 2) {
+          float x0, x1;
+          f2_split(fma_f2(f2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), c2v, nmv), x0, x1);
+          const float p0 = ex2(x0), p1 = ex2(x1);
+          const uint64_t pp = f2(p0, p1);
+          switch ((c >> 1) & 3) {
+            case 0: acc0 = add_f2(acc0, pp); break;
+            case 1: acc1 = add_f2(acc1, pp); break;
+            case 2: acc2 = add_f2(acc2, pp); break;
+            default: acc3 = add_f2(acc3, pp); break;
           }
+          pk[c >> 1] = pack_bf16(p0, p1);
         }
-        const float sum = ((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7]));
-        l += sum;
+        {
+          float u0, u1, u2, u3, u4, u5, u6, u7;
+          f2_split(acc0, u0, u1); f2_split(acc1, u2, u3); f2_split(acc2, u4, u5); f2_split(acc3, u6, u7);
+          l += ((u0 + u1) + (u2 + u3)) + ((u4 + u5) + (u6 + u7));
+        }
+        tm_st32(lane_base + uint32_t(kKT * buf), pk);
         tm_st_wait();
         tc_fence_before();
-        mbar_arrive(p_full);
+        mbar_arrive(&p_full[buf]);
+        ++t;
+        const bool last = it.last_of_item();
+        it.next(a, w_end);
+        if (last) break;
       }
-      if (!ok || !mbar_wait(o_full, item & 1, a.err)) { *abort_flag = 1; break; }
+      if (!ok || !mbar_wait(o_full, item & 1, a.err)) { ok = false; break; }
       tc_fence_after();
       const int qi = i0 + r;
       const float inv = 1.f / l;
@@ -484,7 +539,9 @@ __global__ void __launch_bounds__(kFwdThreads, 2) fmha_fwd_tc_kernel(const __gri
       tc_fence_before();
       mbar_arrive(o_free);
       if (qi < a.q_len) a.lse[(int64_t(b) * a.H + h) * a.q_len + qi] = m + __log2f(l);
+      ++item;
     }
+    if (!ok) *abort_flag = 1;
   }
   // teardown: every role is out of its loop (all waits above are bounded)
   tc_fence_before();
@@ -872,22 +929,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fmha_bwd_tc_kernel(const __gri
         const int lim_hi = __reduce_max_sync(0xffffffffu, lim);
         const int lim_lo = __reduce_min_sync(0xffffffffu, lim);
         uint32_t pp[16], dd[16];
+        // S c - lse, dP - delta and P (dP - delta) as packed fp32 pairs (one
+        // instruction per two columns); exponentials on MUFU (this loop is
+        // bound by instruction issue and latency, as in the forward)
+        const uint64_t c2v = f2(a.c2, a.c2);
         auto half = [&](int h0, const uint32_t* sr, const uint32_t* dr) {
 #pragma unroll
           for (int c = 0; c < 16; c += 4) {
             const int cc = h0 + c;
             const float4 l4 = *reinterpret_cast<const float4*>(sLSE + q0 + cc);
             const float4 d4 = *reinterpret_cast<const float4*>(sDel + q0 + cc);
-            // columns 12..15 of each half on the FMA pipe: the MUFU unit
-            // (16 ex2 per clock per SM) would otherwise bound the pair
-            const float x0 = fmaf(__uint_as_float(sr[c]), a.c2, -l4.x);
-            const float x1 = fmaf(__uint_as_float(sr[c + 1]), a.c2, -l4.y);
-            const float x2 = fmaf(__uint_as_float(sr[c + 2]), a.c2, -l4.z);
-            const float x3 = fmaf(__uint_as_float(sr[c + 3]), a.c2, -l4.w);
-            float p0 = (c == 12) ? ex2_poly(x0) : ex2(x0);
-            float p1 = (c == 12) ? ex2_poly(x1) : ex2(x1);
-            float p2 = (c == 12) ? ex2_poly(x2) : ex2(x2);
-            float p3 = (c == 12) ? ex2_poly(x3) : ex2(x3);
+            float x0, x1, x2, x3;
+            f2_split(fma_f2(f2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), c2v, f2(-l4.x, -l4.y)), x0, x1);
+            f2_split(fma_f2(f2(__uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3])), c2v, f2(-l4.z, -l4.w)), x2, x3);
+            float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
             if (lim_hi > 0) {
               p0 = (cc >= lim) ? p0 : 0.f;
               p1 = (cc + 1 >= lim) ? p1 : 0.f;
@@ -896,9 +951,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fmha_bwd_tc_kernel(const __gri
             }
             pp[cc >> 1] = pack_bf16(p0, p1);
             pp[(cc >> 1) + 1] = pack_bf16(p2, p3);
-            dd[cc >> 1] = pack_bf16(p0 * (__uint_as_float(dr[c]) - d4.x), p1 * (__uint_as_float(dr[c + 1]) - d4.y));
-            dd[(cc >> 1) + 1] =
-                pack_bf16(p2 * (__uint_as_float(dr[c + 2]) - d4.z), p3 * (__uint_as_float(dr[c + 3]) - d4.w));
+            float e0, e1, e2, e3;
+            f2_split(mul_f2(f2(p0, p1), sub_f2(f2(__uint_as_float(dr[c]), __uint_as_float(dr[c + 1])), f2(d4.x, d4.y))),
+                     e0, e1);
+            f2_split(mul_f2(f2(p2, p3),
+                            sub_f2(f2(__uint_as_float(dr[c + 2]), __uint_as_float(dr[c + 3])), f2(d4.z, d4.w))),
+                     e2, e3);
+            dd[cc >> 1] = pack_bf16(e0, e1);
+            dd[(cc >> 1) + 1] = pack_bf16(e2, e3);
           }
         };
         {
@@ -1009,15 +1069,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fmha_bwd_tc_kernel(const __gri
 // ---------------------------------------------------------------------------
 namespace {
 
-// 5-D map over a contiguous [B, T, 3, H, D] bf16 buffer; box = 128 rows of one
-// (b, part, head), swizzled by the row width (64 B for d = 32, 128 B for d = 64).
-CUtensorMap qkv_map(const at::Tensor& qkv) {
+// 5-D map over a contiguous [B, T, 3, H, D] bf16 buffer; box = `rows` rows of
+// one (b, part, head), swizzled by the row width (64 B for d = 32, 128 B for d = 64).
+CUtensorMap qkv_map(const at::Tensor& qkv, int rows = atc::kTile) {
   const int64_t B = qkv.size(0), T = qkv.size(1), H = qkv.size(3), D = qkv.size(4);
   CUtensorMap m;
   cuuint64_t dims[5] = {cuuint64_t(D), cuuint64_t(H), 3, cuuint64_t(T), cuuint64_t(B)};
   cuuint64_t strides[4] = {cuuint64_t(D * 2), cuuint64_t(H * D * 2), cuuint64_t(3 * H * D * 2),
                            cuuint64_t(T * 3 * H * D * 2)};
-  cuuint32_t box[5] = {cuuint32_t(D), 1, 1, cuuint32_t(atc::kTile), 1};
+  cuuint32_t box[5] = {cuuint32_t(D), 1, 1, cuuint32_t(rows), 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   CUresult r = tensor_map_encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, qkv.data_ptr(), dims, strides, box,
                                       estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -1045,19 +1105,19 @@ size_t bwd_smem_bytes(int q_len, int qst) {
 }
 constexpr size_t kSmemCap = 227 * 1024;
 
-template <int D, int STAGES>
-void launch_fwd(const CUtensorMap& tm, const atc::FwdArgs& a) {
-  constexpr size_t used = 1024 + (2 + 2 * STAGES) * atc::Geo<D>::kTileBytes + 256;
+template <int D, int KST>
+void launch_fwd(const CUtensorMap& tq, const CUtensorMap& tkv, const atc::FwdArgs& a) {
+  constexpr size_t used = 1024 + 2 * atc::kTile * atc::Geo<D>::RB + 2 * KST * atc::kKT * atc::Geo<D>::RB + 256;
   // at least 80 KB, so at most two CTAs (two 256-column TMEM allocations) share an SM
   constexpr size_t smem = used > 81920 ? used : 81920;
   static bool attr = false;
   if (!attr) {
-    PD_CHECK_CUDA(cudaFuncSetAttribute(atc::fmha_fwd_tc_kernel<D, STAGES>,
+    PD_CHECK_CUDA(cudaFuncSetAttribute(atc::fmha_fwd_tc_kernel<D, KST>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     attr = true;
   }
   const int grid = a.items < 2 * num_sms() ? a.items : 2 * num_sms();
-  atc::fmha_fwd_tc_kernel<D, STAGES><<<grid, atc::kFwdThreads, smem, stream()>>>(tm, a);
+  atc::fmha_fwd_tc_kernel<D, KST><<<grid, atc::kFwdThreads, smem, stream()>>>(tq, tkv, a);
   PD_CHECK_LAUNCH();
 }
 
@@ -1086,9 +1146,9 @@ std::vector<at::Tensor> fmha_fwd_tc(at::Tensor qkv, int64_t q_len, double scale,
   a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
   a.lse = lse.data_ptr<float>();
   a.err = err.data_ptr<int>();
-  const CUtensorMap tm = qkv_map(qkv);
-  if (D == 32) launch_fwd<32, 3>(tm, a);
-  else launch_fwd<64, 2>(tm, a);
+  const CUtensorMap tq = qkv_map(qkv, atc::kTile), tkv = qkv_map(qkv, atc::kKT);
+  if (D == 32) launch_fwd<32, 6>(tq, tkv, a);
+  else launch_fwd<64, 4>(tq, tkv, a);
   return {o, lse};
 }
 

@@ -59,13 +59,19 @@ class _NativeFMHA(torch.autograd.Function):
         return buf[:, kl - ql:, 0], buf[:, :, 1], buf[:, :, 2], None
 
 
-def _tc_fwd_ok(qkv: torch.Tensor) -> bool:
-    """The tcgen05 forward reads qkv through one TMA map: contiguous, d in {32, 64}.
-    Opt-in (PD_ATTN_TC_FWD=1): on the v6 shapes it measures level with the
-    mma.sync forward, which therefore stays the default."""
+# From this many queries the tcgen05 forward is faster on B200 (v6 pyramid,
+# batch 2048: q 912 / kv 912 4.27 vs 4.52 ms, q 535 / kv 661 2.37 vs 2.44 ms;
+# q 409 / kv 535 1.68 vs 1.66 ms and smaller layers favour the mma.sync kernel).
+_TC_FWD_MIN_Q = int(os.environ.get("PD_ATTN_TC_FWD_MIN_Q", "500"))
+
+
+def _tc_fwd_ok(qkv: torch.Tensor, q_len: int) -> bool:
+    """The tcgen05 forward reads qkv through TMA maps: contiguous, d in {32, 64};
+    used from _TC_FWD_MIN_Q queries up (PD_ATTN_TC_FWD=0: never, =1: always)."""
     g = _ext.gemm()
-    return (hasattr(g, "fmha_fwd_tc") and qkv.is_contiguous() and qkv.shape[-1] in (32, 64)
-            and os.environ.get("PD_ATTN_TC_FWD", "0") == "1")
+    mode = os.environ.get("PD_ATTN_TC_FWD", "")
+    return (hasattr(g, "fmha_fwd_tc") and qkv.is_contiguous() and qkv.shape[-1] in (32, 64) and mode != "0"
+            and (mode == "1" or q_len >= _TC_FWD_MIN_Q))
 
 
 # Below this many queries the mma.sync backward is faster on B200 (v6 pyramid,
@@ -112,7 +118,7 @@ class _NativeFMHAFused(torch.autograd.Function):
         G = _ext.gemm()
         T = qkv.shape[1]
         q, k, v = qkv[:, T - q_len:, 0], qkv[:, :, 1], qkv[:, :, 2]
-        if _tc_fwd_ok(qkv):
+        if _tc_fwd_ok(qkv, q_len):
             o, lse = G.fmha_fwd_tc(qkv, q_len, scale, _err_word(qkv.device))
         else:
             o, lse = G.fmha_fwd(q, k, v, scale)
