@@ -44,8 +44,8 @@ void push_rows(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::T
 void signal_barrier(at::Tensor, int64_t, int64_t, int64_t, at::Tensor);
 void peer_put_row(at::Tensor, at::Tensor, int64_t);
 at::Tensor owner_keys(at::Tensor, at::Tensor, int64_t);
-void peer_reduce_slice(at::Tensor, int64_t, at::Tensor, int64_t, int64_t, double);
-void peer_gather_slices(at::Tensor, int64_t, at::Tensor, at::Tensor);
+void peer_reduce_slice(at::Tensor, int64_t, at::Tensor, int64_t, int64_t, double, int64_t);
+void peer_gather_slices(at::Tensor, int64_t, at::Tensor, at::Tensor, int64_t, int64_t);
 }  // namespace pd
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -78,7 +78,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("signal_barrier", &pd::signal_barrier);
   m.def("peer_put_row", &pd::peer_put_row, "row `rank` of every rank's int64 [W, n] board = src (peer stores)");
   m.def("owner_keys", &pd::owner_keys);
-  m.def("peer_reduce_slice", &pd::peer_reduce_slice, "own[a:b) = scale * sum over ranks of peer[a:b) (NVLink P2P loads)");
-  m.def("peer_gather_slices", &pd::peer_gather_slices, "copy every other rank's slice from that rank (all-gather)");
+  m.def("peer_reduce_slice", &pd::peer_reduce_slice, py::arg("ptrs"), py::arg("rank"), py::arg("own"), py::arg("a"),
+        py::arg("b"), py::arg("scale"), py::arg("max_blocks") = 0,
+        "own[a:b) = scale * sum over ranks of peer[a:b) (NVLink P2P loads); max_blocks > 0 caps the grid");
+  m.def("peer_gather_slices", &pd::peer_gather_slices, py::arg("ptrs"), py::arg("rank"), py::arg("own"),
+        py::arg("bounds"), py::arg("span") = 0, py::arg("max_blocks") = 0,
+        "copy every other rank's slice [bounds[q], bounds[q+1]) from that rank (all-gather); span sizes the grid");
   m.def("launch_count", &pd::launches, "kernels launched by this extension so far");
 }

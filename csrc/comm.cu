@@ -290,26 +290,32 @@ static PeerBufs peer_bufs(const at::Tensor& ptrs, int64_t rank) {
 }
 
 // own[a:b) = scale * sum_r peer_r[a:b); a, b multiples of 4.
-void peer_reduce_slice(at::Tensor ptrs, int64_t rank, at::Tensor own, int64_t a, int64_t b, double scale) {
+// max_blocks > 0 caps the grid (a collective overlapped with compute takes a
+// few SMs' worth of CTAs instead of the whole GPU).
+void peer_reduce_slice(at::Tensor ptrs, int64_t rank, at::Tensor own, int64_t a, int64_t b, double scale,
+                       int64_t max_blocks) {
   TORCH_CHECK(own.is_cuda() && own.scalar_type() == at::kFloat && own.is_contiguous());
   TORCH_CHECK(a >= 0 && b <= own.numel() && a % 4 == 0 && b % 4 == 0 && a <= b, "slice must be 4-aligned");
   const PeerBufs P = peer_bufs(ptrs, rank);
   if (b == a) return;
   int64_t blocks = ((b - a) / 4 + 511) / 512;
-  const int64_t cap = int64_t(num_sms()) * 4;
+  const int64_t cap = max_blocks > 0 ? max_blocks : int64_t(num_sms()) * 4;
   if (blocks > cap) blocks = cap;
   peer_reduce_slice_kernel<<<blocks, 512, 0, stream()>>>(P, own.data_ptr<float>(), a, b, float(scale));
   PD_CHECK_LAUNCH();
 }
 
 // own[slice q] = peer_q[slice q] for every q != rank; bounds: int64 CUDA [W + 1].
-void peer_gather_slices(at::Tensor ptrs, int64_t rank, at::Tensor own, at::Tensor bounds) {
+void peer_gather_slices(at::Tensor ptrs, int64_t rank, at::Tensor own, at::Tensor bounds, int64_t span,
+                        int64_t max_blocks) {
   TORCH_CHECK(own.is_cuda() && own.scalar_type() == at::kFloat && own.is_contiguous());
   TORCH_CHECK(bounds.is_cuda() && bounds.scalar_type() == at::kLong && bounds.numel() == ptrs.numel() + 1);
   const PeerBufs P = peer_bufs(ptrs, rank);
-  const int64_t per = own.numel() / P.world + 1;
+  // span: elements the bounds cover (0: the whole buffer), sizes the grid
+  const int64_t per = (span > 0 ? span : own.numel()) / P.world + 1;
   int64_t blocks = (per / 4 + 511) / 512;
-  const int64_t cap = int64_t(num_sms()) * 4 / (P.world > 1 ? P.world - 1 : 1) + 1;
+  const int64_t cap = max_blocks > 0 ? (max_blocks + P.world - 2) / (P.world > 1 ? P.world - 1 : 1)
+                                     : int64_t(num_sms()) * 4 / (P.world > 1 ? P.world - 1 : 1) + 1;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   peer_gather_slices_kernel<<<dim3(unsigned(blocks), unsigned(P.world)), 512, 0, stream()>>>(

@@ -173,11 +173,6 @@ class AutoSplitTokenizer(nn.Module):
 
 
 class OneTransModel(BaseModel):
-    # the embedding lookup is the first op of the forward, so its backward runs
-    # after every dense gradient is final (the engine overlaps the dense
-    # gradient all-reduce with the sparse exchange on that basis)
-    lookup_first = True
-
     def __init__(self, config: Config, device: torch.device | None = None, meta_device: bool = False):
         super().__init__()
         self.config = config

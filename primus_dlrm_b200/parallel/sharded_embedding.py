@@ -383,7 +383,6 @@ class PeerExecutor:
         self.plan_pads = torch.tensor(self.plan_buf.ptrs, dtype=torch.int64)
         self.plan_boards = torch.tensor([p + 64 * 8 if p else 0 for p in self.plan_buf.ptrs], dtype=torch.int64)
         self.side = torch.cuda.Stream(device)
-        self.pre_backward = None   # called when the backward starts (the engine's dense-sync overlap)
         self.barrier()
 
     # -- primitives --------------------------------------------------------
@@ -557,8 +556,6 @@ class PeerExecutor:
         """Local reduction per unique row, push to the owners, owner update.
         Without a plan from the forward (a lookup run outside autograd) the
         plan is made here."""
-        if self.pre_backward is not None:
-            self.pre_backward()
         if plan is None:
             plan = self._plan_core(spec, ids, grads)
             self._plan_counts(plan, torch.cuda.current_stream(self.device))

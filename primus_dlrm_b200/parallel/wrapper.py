@@ -21,6 +21,7 @@ kernels, CUDA) or ``nccl`` (collective baseline; also the CPU/gloo path).
 from __future__ import annotations
 
 import logging
+import os
 
 import torch
 import torch.distributed as dist
@@ -130,11 +131,11 @@ class _PeerDense:
     def reduce_scatter(self, scale: float) -> None:
         a, b = self.slice
         self.barrier()
-        self.C.peer_reduce_slice(self.ptrs, self.rank, self.buf, a, b, scale)
+        self.C.peer_reduce_slice(self.ptrs, self.rank, self.buf, a, b, scale, 0)
 
     def all_gather(self) -> None:
         self.barrier()
-        self.C.peer_gather_slices(self.ptrs, self.rank, self.buf, self.bounds)
+        self.C.peer_gather_slices(self.ptrs, self.rank, self.buf, self.bounds, 0, 0)
         self.barrier()
 
 
@@ -142,17 +143,66 @@ class PeerGradSync(_PeerDense):
     """DDP gradient averaging over NVLink peer memory (two-shot all-reduce:
     each rank reduces its 1/W slice from every peer's arena, then gathers the
     other slices). The flat gradient arena itself lives in the shared buffer
-    (``bind``), so backward writes straight into memory the peers read."""
+    (``bind``), so backward writes straight into memory the peers read.
 
-    def __init__(self, numel: int, device: torch.device, group=None, timeout_s: float = 60.0):
+    Overlap with the backward (the reference's bucketed DDP,
+    ``primus_dlrm/distributed/wrapper.py:61-64``): the arena is cut into
+    buckets of about ``PD_DDP_BUCKET_MB`` (default 32) MB in reverse parameter
+    order, the order in which the backward produces the gradients. A
+    post-accumulate-grad hook on every parameter counts the gradients a bucket
+    still waits for; when the count reaches zero the bucket's reduce-scatter
+    and all-gather are launched on a side stream, right behind the kernels
+    that wrote its last gradient. Buckets launch strictly in index order, so
+    every rank issues the same sequence of collectives. ``finish`` launches
+    the buckets whose parameters got no gradient this step and makes the
+    compute stream wait for the side stream.
+    """
+
+    BLOCKS = 32          # CTAs per overlapped reduce / gather: the backward keeps the rest of the GPU
+
+    def __init__(self, numel: int, device: torch.device, group=None, timeout_s: float = 60.0,
+                 bucket_mb: float | None = None):
         super().__init__(numel, device, group, timeout_s)
         self._side = None
-        self._pending = False
+        self.bucket_mb = float(os.environ.get("PD_DDP_BUCKET_MB", "32")) if bucket_mb is None else bucket_mb
+        self.buckets: list[tuple[int, int, int, int, torch.Tensor]] = []   # (lo, hi, a, b, bounds)
+        self._bucket_params: list[int] = []
+        self._hooks = []
+        self._armed = False
+        self._left: list[int] = []
+        self._launched = 0
 
     def bind(self, flat) -> None:
         self.buf.copy_(flat.grad)
         flat.grad = self.buf
         flat.zero_grad()
+        if hasattr(flat, "params") and hasattr(flat, "offsets"):
+            self._build_buckets(flat)
+
+    def _build_buckets(self, flat) -> None:
+        cap = max(int(self.bucket_mb * 2 ** 20 / 4), 64)
+        sizes = [(p.numel() + 63) // 64 * 64 for p in flat.params]
+        groups, cur, size = [], [], 0
+        for i in reversed(range(len(flat.params))):
+            cur.append(i)
+            size += sizes[i]
+            if size >= cap:
+                groups.append(cur)
+                cur, size = [], 0
+        if cur:
+            groups.append(cur)
+        dev = self.buf.device
+        for k, idx in enumerate(groups):
+            lo = min(flat.offsets[i] for i in idx)
+            hi = min(max(flat.offsets[i] + sizes[i] for i in idx), self.numel)
+            per = (-(-(hi - lo) // self.world) + 63) // 64 * 64
+            b = [min(lo + r * per, hi) for r in range(self.world + 1)]
+            self.buckets.append((lo, hi, b[self.rank], b[self.rank + 1],
+                                 torch.tensor(b, dtype=torch.int64, device=dev)))
+            self._bucket_params.append(len(idx))
+            for i in idx:
+                self._hooks.append(flat.params[i].register_post_accumulate_grad_hook(
+                    lambda _p, k=k: self._on_grad(k)))
 
     def sync(self, flat_grad: torch.Tensor) -> None:
         if flat_grad.data_ptr() != self.buf.data_ptr():
@@ -162,32 +212,47 @@ class PeerGradSync(_PeerDense):
         if flat_grad.data_ptr() != self.buf.data_ptr():
             flat_grad.copy_(self.buf)
 
-    # -- overlap with the sparse exchange ---------------------------------
-    def start_async(self, flat_grad: torch.Tensor) -> bool:
-        """Start the all-reduce on a side stream once every dense gradient is
-        final (the embedding lookup's backward runs last, after all of them),
-        so it overlaps the sparse exchange on the compute stream. Returns
-        False (nothing started) when the arena is not the shared buffer."""
-        if self._pending:
-            return True                       # already started this step
-        if flat_grad.data_ptr() != self.buf.data_ptr() or not flat_grad.is_cuda:
+    # -- overlap with the backward -----------------------------------------
+    def begin(self) -> bool:
+        """Arm the bucket hooks for one backward; False when there are no buckets."""
+        if not self.buckets or not self.buf.is_cuda:
             return False
-        main = torch.cuda.current_stream(flat_grad.device)
         if self._side is None:
-            self._side = torch.cuda.Stream(flat_grad.device)
-        self._side.wait_stream(main)
-        with torch.cuda.stream(self._side):
-            self.reduce_scatter(1.0 / self.world)
-            self.all_gather()
-        self._pending = True
+            self._side = torch.cuda.Stream(self.buf.device)
+        self._left = list(self._bucket_params)
+        self._launched = 0
+        self._armed = True
         return True
 
-    def finish_async(self) -> bool:
-        """Make the compute stream wait for a started all-reduce; False if none."""
-        if not self._pending:
+    def _on_grad(self, k: int) -> None:
+        if not self._armed:
+            return
+        self._left[k] -= 1
+        while self._launched < len(self.buckets) and self._left[self._launched] <= 0:
+            self._launch(self._launched)
+            self._launched += 1
+
+    def _launch(self, k: int) -> None:
+        lo, hi, a, b, bounds = self.buckets[k]
+        self._side.wait_stream(torch.cuda.current_stream(self.buf.device))
+        with torch.cuda.stream(self._side):
+            self.barrier()                                  # every rank's bucket k is final
+            self.C.peer_reduce_slice(self.ptrs, self.rank, self.buf, a, b, 1.0 / self.world, self.BLOCKS)
+            self.barrier()                                  # every slice of bucket k is reduced
+            self.C.peer_gather_slices(self.ptrs, self.rank, self.buf, bounds, hi - lo, self.BLOCKS)
+
+    def finish(self) -> bool:
+        """Launch the buckets not started during the backward, then make the
+        compute stream wait for all of them. False if ``begin`` was not called."""
+        if not self._armed:
             return False
+        self._armed = False
+        for k in range(self._launched, len(self.buckets)):
+            self._launch(k)
+        self._launched = len(self.buckets)
+        with torch.cuda.stream(self._side):
+            self.barrier()               # peers have finished reading this rank's arena
         torch.cuda.current_stream(self.buf.device).wait_stream(self._side)
-        self._pending = False
         return True
 
 

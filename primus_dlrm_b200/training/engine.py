@@ -101,18 +101,15 @@ class TrainEngine:
         self.flat.zero_grad()
         with phase("pd.forward"), torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.use_amp):
             total, task_losses = self.compute_loss(batch)
-        ex = self._overlap_executor()
-        if ex is not None:
-            # the dense all-reduce starts when the lookup's backward begins (every
-            # dense gradient is final by then) and runs beside the sparse exchange
-            ex.pre_backward = lambda: self.grad_sync.start_async(self.flat.grad)
+        # dense gradient sync overlapped with the backward: buckets of the flat
+        # gradient arena are all-reduced as soon as their last gradient is written
+        bucketed = self._bucketed_sync()
+        overlapped = bucketed is not None and bucketed.begin()
         with phase("pd.backward"):
             total.backward()
-        if ex is not None:
-            ex.pre_backward = None
         if self.grad_sync is not None:
             with phase("pd.dense_sync"):
-                if not (ex is not None and self.grad_sync.finish_async()):
+                if not (overlapped and bucketed.finish()):
                     self.grad_sync.sync(self.flat.grad)
         with phase("pd.optimizer"):
             if tc.nan_guard and not bool(torch.isfinite(total)):
@@ -126,22 +123,15 @@ class TrainEngine:
         self.global_step += 1
         return total.detach(), task_losses
 
-    def _overlap_executor(self):
-        """The peer exchange executor when the dense sync can overlap it: the
-        model's embedding lookup must be the first op of its forward
-        (``lookup_first``), so its backward runs after every dense gradient
-        has been accumulated."""
+    def _bucketed_sync(self):
+        """The peer-memory gradient sync when its per-bucket overlap with the
+        backward is on (``PD_OVERLAP_DENSE_SYNC=0``: one all-reduce after the
+        backward instead)."""
         gs = self.grad_sync
         if gs is None or os.environ.get("PD_OVERLAP_DENSE_SYNC", "1") == "0":
             return None
-        inner = self._inner()
-        if not getattr(inner, "lookup_first", False):
-            return None
         impl = getattr(gs, "impl", None) or gs
-        if not hasattr(impl, "start_async"):
-            return None
-        ex = getattr(getattr(inner, "emb", None), "executor", None)
-        return ex if ex is not None and hasattr(ex, "pre_backward") else None
+        return impl if hasattr(impl, "begin") and hasattr(impl, "finish") else None
 
     def step_host(self, packed: PackedBatch) -> float:
         """End-to-end step through the public API: pinned host batch -> H2D

@@ -1,6 +1,8 @@
-"""Multi-GPU (2 ranks, NCCL): the NVLink peer-memory sparse exchange against
-the collective baseline, and a short OneTrans training run through the full
-sharded stack.  Needs 2+ CUDA devices."""
+"""Multi-GPU (every visible GPU up to 8, at least 2; NCCL): the NVLink
+peer-memory sparse exchange against the collective baseline, the dense peer
+collectives against NCCL, the bucketed gradient sync overlapped with the
+backward against the sync after it, and a bounded barrier.  Needs 2+ CUDA
+devices."""
 import os
 
 import pytest
@@ -63,6 +65,10 @@ def run_nccl(fn, world=2):
     return res
 
 
+def _world() -> int:
+    return min(torch.cuda.device_count(), 8)
+
+
 def _cfg(comm, opt="sgd"):
     from primus_dlrm_b200.config import Config, TableShardingSpec
     cfg = Config.load(TINY)
@@ -114,8 +120,8 @@ def _peer_vs_nccl(rank, world):
 def test_peer_exchange_matches_collective_baseline():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    res = run_nccl(_peer_vs_nccl, 2)
-    for r in (0, 1):
+    res = run_nccl(_peer_vs_nccl, _world())
+    for r in range(_world()):
         lp, ln = res[r]["peer"][0], res[r]["nccl"][0]
         assert lp == pytest.approx(ln, rel=2e-3, abs=2e-3)
     sd_p, sd_n = res[0]["peer"][1], res[0]["nccl"][1]
@@ -205,7 +211,62 @@ def _dense_peer_collectives(rank, world):
 def test_dense_peer_collectives_match_nccl():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    res = run_nccl(_dense_peer_collectives, 2)
+    res = run_nccl(_dense_peer_collectives, _world())
     for r, d in res.items():
         for k, v in d.items():
             assert v < 1e-5, (r, k, v)
+
+
+def _overlap_vs_sync(rank, world):
+    """The same steps with the bucketed gradient sync overlapped with the
+    backward (many small buckets) and with one all-reduce after it."""
+    import copy
+
+    import torch.distributed as dist
+
+    from primus_dlrm_b200.data.synthetic import generate_batch
+    from primus_dlrm_b200.parallel.build import build_model
+    from primus_dlrm_b200.parallel.state import full_state_dict, load_full_state_dict
+    from primus_dlrm_b200.parallel.wrapper import wrap_model
+    from primus_dlrm_b200.training.engine import TrainEngine
+    dev = torch.device("cuda", rank)
+    torch.manual_seed(0)
+    init = copy.deepcopy(build_model(_cfg("peer")).state_dict())
+    out = {}
+    for mode in ("1", "0"):
+        os.environ["PD_OVERLAP_DENSE_SYNC"] = mode
+        os.environ["PD_DDP_BUCKET_MB"] = "0.05"        # tens of buckets on the tiny model
+        cfg = _cfg("peer")
+        model = build_model(cfg, device=dev, meta_device=True)
+        model, sync = wrap_model(model, dev, cfg)
+        load_full_state_dict(model, init)
+        eng = TrainEngine(model, cfg, dev, grad_sync=sync)
+        if mode == "1":
+            out["buckets"] = len(sync.impl.buckets)
+        losses = []
+        for s in range(3):
+            b = generate_batch(cfg, 32, seed=1000 * s + rank)
+            loss, _ = eng.step({k: v.to(dev) for k, v in b.items()})
+            losses.append(float(loss))
+        torch.cuda.synchronize()
+        sync.impl.check()
+        sd = full_state_dict(model)
+        out[mode] = (losses, {k: v for k, v in sd.items() if not k.startswith("emb.")})
+        dist.barrier()
+    os.environ.pop("PD_OVERLAP_DENSE_SYNC", None)
+    os.environ.pop("PD_DDP_BUCKET_MB", None)
+    return out
+
+
+def test_overlapped_bucket_sync_matches_sync_after_backward():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = run_nccl(_overlap_vs_sync, _world())
+    assert res[0]["buckets"] > 4
+    # not bitwise: the sparse exchange's atomics already perturb the first
+    # loss (before any gradient sync) in the last bits between two runs
+    for r, d in res.items():
+        assert d["1"][0] == pytest.approx(d["0"][0], rel=1e-4, abs=1e-5), (r, d["1"][0], d["0"][0])
+    sd1, sd0 = res[0]["1"][1], res[0]["0"][1]
+    for k in sd0:
+        torch.testing.assert_close(sd1[k], sd0[k], rtol=1e-3, atol=1e-5, msg=lambda m: f"{k}: {m}")
