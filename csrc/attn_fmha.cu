@@ -538,11 +538,11 @@ __global__ void fmha_bwd_dq_kernel(const float* __restrict__ dq_acc, __nv_bfloat
 // host
 // ---------------------------------------------------------------------------
 static void check_qkv(const at::Tensor& t, const char* name) {
-  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, " must be a bf16 CUDA tensor");
-  TORCH_CHECK(t.dim() == 4 && t.stride(3) == 1, name, " must be [B, L, H, d] with unit stride on d");
-  TORCH_CHECK(t.stride(2) == t.size(3), name, ": heads must be contiguous (stride d)");
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0 && t.stride(1) % 8 == 0 && t.stride(0) % 8 == 0,
-              name, ": rows must be 16-byte aligned");
+  PD_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, "%s must be a bf16 CUDA tensor", name);
+  PD_CHECK(t.dim() == 4 && t.stride(3) == 1, "%s must be [B, L, H, d] with unit stride on d", name);
+  PD_CHECK(t.stride(2) == t.size(3), "%s: heads must be contiguous (stride d)", name);
+  PD_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0 && t.stride(1) % 8 == 0 && t.stride(0) % 8 == 0,
+           "%s: rows must be 16-byte aligned", name);
 }
 
 // q [B, q_len, H, d] (view), k/v [B, kv_len, H, d] (views) -> (o [B, q_len, H, d], lse [B, H, q_len])

@@ -1083,7 +1083,7 @@ CUtensorMap qkv_map(const at::Tensor& qkv, int rows = atc::kTile) {
                                       estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                       D == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled(qkv) failed: ", int(r));
+  PD_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled(qkv) failed: %d", int(r));
   return m;
 }
 
@@ -1194,7 +1194,7 @@ void fmha_bwd_tc(at::Tensor qkv, at::Tensor o, at::Tensor lse, at::Tensor dout, 
     CUresult r = tensor_map_encode_tiled(&td, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, dout.data_ptr(), dims, strides, box,
                                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                                         CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled(dout) failed: ", int(r));
+    PD_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled(dout) failed: %d", int(r));
   }
   // three Q / dO stages where the dQ block leaves room for them, else two
   const int grid = a.items < num_sms() ? a.items : num_sms();

@@ -42,7 +42,7 @@ at::Tensor ipc_handle(at::Tensor t) {
   CUdeviceptr base = 0;
   size_t size = 0;
   CUresult r = mem_get_address_range(&base, &size, reinterpret_cast<CUdeviceptr>(t.data_ptr()));
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuMemGetAddressRange failed: ", int(r));
+  PD_CHECK(r == CUDA_SUCCESS, "cuMemGetAddressRange failed: %d", int(r));
   cudaIpcMemHandle_t h;
   PD_CHECK_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
   auto out = at::empty({int64_t(sizeof(h) + 8)}, at::TensorOptions().dtype(at::kByte));

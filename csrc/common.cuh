@@ -16,14 +16,28 @@
 #include <c10/cuda/CUDAStream.h>
 #include <c10/util/Exception.h>
 #include <atomic>
+#include <cstdio>
 #include <optional>
 #include <vector>
+
+// Checks in the nvcc-compiled sources format their message with snprintf and
+// hand TORCH_CHECK one C string: a message assembled by c10::str from several
+// parts (C++ streams) crashed the process with SIGSEGV in these translation
+// units when the check failed, instead of raising (a failing check with a
+// single-string message raises normally).
+#define PD_CHECK(cond, ...)                                                        \
+  do {                                                                             \
+    if (C10_UNLIKELY(!(cond))) {                                                   \
+      char pd_msg__[512];                                                          \
+      snprintf(pd_msg__, sizeof(pd_msg__), __VA_ARGS__);                           \
+      TORCH_CHECK(false, static_cast<const char*>(pd_msg__));                      \
+    }                                                                              \
+  } while (0)
 
 #define PD_CHECK_CUDA(expr)                                                        \
   do {                                                                             \
     cudaError_t err__ = (expr);                                                    \
-    TORCH_CHECK(err__ == cudaSuccess, "CUDA error ", cudaGetErrorString(err__),    \
-                " at ", __FILE__, ":", __LINE__);                                  \
+    PD_CHECK(err__ == cudaSuccess, "CUDA error %s at %s:%d", cudaGetErrorString(err__), __FILE__, __LINE__); \
   } while (0)
 
 #define PD_CHECK_LAUNCH() do { PD_CHECK_CUDA(cudaGetLastError()); ::pd::note_launch(); } while (0)

@@ -5,6 +5,7 @@
 // clear error only when a driver call is actually made.
 #pragma once
 
+#include <cstdio>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <torch/extension.h>
@@ -16,8 +17,11 @@ inline Fn driver_entry(const char* name) {
   void* p = nullptr;
   cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
   const cudaError_t e = cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q);
-  TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr,
-              "CUDA driver entry point ", name, " is unavailable (", int(e), ", ", int(q), ")");
+  if (!(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr)) {
+    char msg[256];   // one C string: see PD_CHECK in common.cuh
+    snprintf(msg, sizeof(msg), "CUDA driver entry point %s is unavailable (%d, %d)", name, int(e), int(q));
+    TORCH_CHECK(false, static_cast<const char*>(msg));
+  }
   return reinterpret_cast<Fn>(p);
 }
 

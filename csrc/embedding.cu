@@ -29,7 +29,7 @@
 namespace pd {
 
 constexpr int kMaxSlots = 48;
-constexpr int kMaxTables = 24;
+constexpr int kMaxTables = 32;
 constexpr int kChunk = 32;  // sorted positions per warp in the backward
 
 struct Slot {
@@ -733,7 +733,7 @@ static void fill_tables(GatherParams& P, const std::vector<at::Tensor>& weights,
                         const std::vector<at::Tensor>& state1,
                         const std::vector<at::Tensor>& state2, const at::Tensor& meta) {
   const int nt = static_cast<int>(weights.size());
-  TORCH_CHECK(nt <= kMaxTables, "too many tables in one launch: ", nt);
+  PD_CHECK(nt <= kMaxTables, "too many tables in one launch: %d (at most %d)", nt, kMaxTables);
   TORCH_CHECK(meta.device().is_cpu() && meta.dtype() == at::kLong && meta.size(0) == nt && meta.size(1) == 6);
   auto m = meta.accessor<int64_t, 2>();
   P.n_tables = nt;
@@ -757,7 +757,7 @@ static at::ScalarType fill_slots(GatherParams& P, const std::vector<at::Tensor>&
                                  const std::vector<at::Tensor>& io, const at::Tensor& slot_meta,
                                  const std::vector<at::Tensor>& offsets, bool pooled_allowed) {
   const int ns = static_cast<int>(ids.size());
-  TORCH_CHECK(ns >= 1 && ns <= kMaxSlots, "slot count out of range: ", ns);
+  PD_CHECK(ns >= 1 && ns <= kMaxSlots, "slot count out of range: %d (1 .. %d)", ns, kMaxSlots);
   TORCH_CHECK(io.size() == ids.size());
   TORCH_CHECK(slot_meta.device().is_cpu() && slot_meta.dtype() == at::kLong &&
               slot_meta.size(0) == ns && slot_meta.size(1) == 4);

@@ -12,7 +12,7 @@ void fmha_bwd_tc(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int
                  c10::optional<at::Tensor>);
 int64_t fmha_bwd_tc_max_q();
 void tc_gemm(at::Tensor, at::Tensor, at::Tensor, int64_t, c10::optional<at::Tensor>, c10::optional<at::Tensor>,
-             at::Tensor, bool);
+             at::Tensor, bool, c10::optional<at::Tensor>);
 void tc_wgrad(at::Tensor, at::Tensor, at::Tensor, at::Tensor, bool);
 at::Tensor tc_mma_rate(int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, at::Tensor);
 at::Tensor tc_mma_burst(int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, at::Tensor);
@@ -30,7 +30,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fmha_bwd", &pd::fmha_bwd, "pyramid causal attention backward into dq/dk/dv views");
   m.def("tc_gemm", &pd::tc_gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("epi") = 0,
         py::arg("R") = py::none(), py::arg("AUX") = py::none(), py::arg("err"), py::arg("b_kn") = false,
-        "C[l] = epi(A[l] @ B[l]^T) on tcgen05 (A [L,M,K], B [L|1,N,K] or with b_kn [L|1,K,N], C [L,M,N] bf16 views)");
+        py::arg("R2") = py::none(),
+        "C[l] = epi(A[l] @ B[l]^T) on tcgen05 (A [L,M,K], B [L|1,N,K] or with b_kn [L|1,K,N], C [L,M,N] bf16 views); "
+        "epi 0 none, 1 gelu, 2 +R, 3 dgelu(R), 4 gelu+gelu' to AUX, 5 *R, 6 relu(+R), 7 acc where R>0, 8 R*acc+R2");
   m.def("tc_wgrad", &pd::tc_wgrad, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("err"), py::arg("l_sum") = false,
         "C[l] (fp32, zeroed) += A[l]^T B[l] over rows on tcgen05, split over rows (A [L,K,M], B [L,K,N] bf16 views); "
         "l_sum: one C summed over the batches too");

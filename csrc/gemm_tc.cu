@@ -47,7 +47,14 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;
 // kGeluD: C = GELU(x), AUX = GELU'(x) for x = bf16(acc + R) -- the derivative
 // stored in the forward makes the backward's epilogue a plain product (kMul:
 // C = acc * R), with no transcendental per element.
-enum Epi : int { kNone = 0, kGelu = 1, kResidual = 2, kDGelu = 3, kGeluD = 4, kMul = 5 };
+// kRelu: C = max(acc + R, 0) (R: a bias through a zero row stride);
+// kMaskPos: C = acc where R > 0, else 0 (R: the ReLU layer's stored output,
+// so the data gradient of the next layer leaves as the pre-activation
+// gradient of this one); kMulAdd: C = R * (acc + b) + R2, with b added via
+// the operands (an extra K row), AUX optionally storing acc (the DCNv2 cross
+// layer: x_{l+1} = x0 * (t V + b) + x_l with R = x0, R2 = x_l).
+enum Epi : int { kNone = 0, kGelu = 1, kResidual = 2, kDGelu = 3, kGeluD = 4, kMul = 5, kRelu = 6, kMaskPos = 7,
+                 kMulAdd = 8 };
 
 struct Params {
   int M, N, K, L;
@@ -55,6 +62,7 @@ struct Params {
   __nv_bfloat16* C; int64_t c_ls, c_ms;
   const __nv_bfloat16* R; int64_t r_ls, r_ms;      // addend, pre-activation (kDGelu) or factor (kMul)
   __nv_bfloat16* AUX; int64_t aux_ls, aux_ms;       // pre-activation (kGelu, optional) or GELU' (kGeluD)
+  const __nv_bfloat16* R2; int64_t r2_ls, r2_ms;    // second addend (kMulAdd)
   int epi;
   int a_mode, b_mode;   // TMA map dim order: 0 = {K, rows, L}, 1 = {K, L, rows}
   int c_mode, x_mode;   // store maps of C / AUX: 0 = {N, rows, L}, 1 = {N, L, rows}
@@ -438,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        if (has_r && p.epi != kDGelu && p.epi != kMul) {
+        if (has_r && p.epi != kDGelu && p.epi != kMul && p.epi != kMaskPos && p.epi != kMulAdd) {
           // addend before the activation: residual, or a bias broadcast through a zero row stride
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -500,6 +508,53 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
               v[8 * j + 2 * e + 1] *= f.y;
             }
           }
+        } else if (p.epi == kRelu) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+        } else if (p.epi == kMaskPos) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 pk = *reinterpret_cast<const uint4*>(stR + sw(lane, j));
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&pk);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __bfloat1622float2(h[e]);
+              v[8 * j + 2 * e] = f.x > 0.f ? v[8 * j + 2 * e] : 0.f;
+              v[8 * j + 2 * e + 1] = f.y > 0.f ? v[8 * j + 2 * e + 1] : 0.f;
+            }
+          }
+        } else if (p.epi == kMulAdd) {
+          // R2 row of this thread: 32 columns straight from global memory
+          const int row = m0 + lane;
+          uint4 q4[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
+                         make_uint4(0, 0, 0, 0)};
+          if (row < p.M) {
+            const uint4* src = reinterpret_cast<const uint4*>(p.R2 + l * p.r2_ls + int64_t(row) * p.r2_ms + n0 + c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) q4[j] = __ldcs(src + j);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 pk = *reinterpret_cast<const uint4*>(stR + sw(lane, j));
+            if (p.AUX) {   // acc to AUX, in the 16 bytes of R this thread has just read
+              uint4 ax;
+              __nv_bfloat162 a0 = __floats2bfloat162_rn(v[8 * j], v[8 * j + 1]);
+              __nv_bfloat162 a1 = __floats2bfloat162_rn(v[8 * j + 2], v[8 * j + 3]);
+              __nv_bfloat162 a2 = __floats2bfloat162_rn(v[8 * j + 4], v[8 * j + 5]);
+              __nv_bfloat162 a3 = __floats2bfloat162_rn(v[8 * j + 6], v[8 * j + 7]);
+              ax.x = *reinterpret_cast<uint32_t*>(&a0); ax.y = *reinterpret_cast<uint32_t*>(&a1);
+              ax.z = *reinterpret_cast<uint32_t*>(&a2); ax.w = *reinterpret_cast<uint32_t*>(&a3);
+              *reinterpret_cast<uint4*>(stX + sw(lane, j)) = ax;
+            }
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&pk);
+            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&q4[j]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __bfloat1622float2(h[e]), g = __bfloat1622float2(h2[e]);
+              v[8 * j + 2 * e] = fmaf(f.x, v[8 * j + 2 * e], g.x);
+              v[8 * j + 2 * e + 1] = fmaf(f.y, v[8 * j + 2 * e + 1], g.y);
+            }
+          }
         } else if (p.epi == kDGelu) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -528,7 +583,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         __syncwarp();
         if (lane == 0) {
           tma_store_rows(&tmC, stC, p.c_mode, n0 + c, m0, l);
-          if ((p.epi == kGelu || p.epi == kGeluD) && p.AUX) tma_store_rows(&tmX, stX, p.x_mode, n0 + c, m0, l);
+          if ((p.epi == kGelu || p.epi == kGeluD || p.epi == kMulAdd) && p.AUX)
+            tma_store_rows(&tmX, stX, p.x_mode, n0 + c, m0, l);
           bulk_commit();
         }
         ++kc;
@@ -764,14 +820,16 @@ namespace {
 // 1..256 elements.
 void check_encode(const void* base, const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
                   int rank, const char* what) {
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, what, ": base address not 16-byte aligned");
+  PD_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "%s: base address not 16-byte aligned", what);
   for (int i = 0; i < rank; ++i) {
-    TORCH_CHECK(dims[i] >= 1 && dims[i] < (cuuint64_t(1) << 32), what, ": extent ", i, " out of range (", dims[i], ")");
-    TORCH_CHECK(box[i] >= 1 && box[i] <= 256, what, ": box ", i, " out of range (", box[i], ")");
+    PD_CHECK(dims[i] >= 1 && dims[i] < (cuuint64_t(1) << 32), "%s: extent %d out of range (%llu)", what, i,
+             (unsigned long long)dims[i]);
+    PD_CHECK(box[i] >= 1 && box[i] <= 256, "%s: box %d out of range (%u)", what, i, (unsigned)box[i]);
   }
   for (int i = 0; i + 1 < rank; ++i)
-    TORCH_CHECK(strides[i] % 16 == 0 && strides[i] > 0 && strides[i] < (cuuint64_t(1) << 40), what, ": stride ", i,
-                " (", strides[i], " bytes) must be a positive multiple of 16 below 2^40");
+    PD_CHECK(strides[i] % 16 == 0 && strides[i] > 0 && strides[i] < (cuuint64_t(1) << 40),
+             "%s: stride %d (%llu bytes) must be a positive multiple of 16 below 2^40", what, i,
+             (unsigned long long)strides[i]);
 }
 
 // Every element a [L, rows, K] view addresses lies inside its storage (a TMA
@@ -781,11 +839,11 @@ void check_extent(const at::Tensor& t, const char* name) {
   if (t.numel() == 0) return;
   int64_t last = t.storage_offset();
   for (int64_t d = 0; d < t.dim(); ++d) {
-    TORCH_CHECK(t.stride(d) >= 0, name, ": negative strides are not supported");
+    PD_CHECK(t.stride(d) >= 0, "%s: negative strides are not supported", name);
     last += (t.size(d) - 1) * t.stride(d);
   }
-  TORCH_CHECK(int64_t((last + 1) * t.element_size()) <= int64_t(t.storage().nbytes()), name,
-              ": the view reaches past the end of its storage");
+  PD_CHECK(int64_t((last + 1) * t.element_size()) <= int64_t(t.storage().nbytes()),
+           "%s: the view reaches past the end of its storage", name);
 }
 
 CUtensorMap make_map(const void* base, int64_t K, int64_t rows, int64_t L, int64_t row_stride, int64_t l_stride,
@@ -809,8 +867,8 @@ CUtensorMap make_map(const void* base, int64_t K, int64_t rows, int64_t L, int64
   CUresult r = tensor_map_encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
                                       box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", int(r), "): K=", K, " rows=", rows, " L=", L,
-              " row_stride=", row_stride, " l_stride=", l_stride);
+  PD_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (%d): K=%lld rows=%lld L=%lld row_stride=%lld l_stride=%lld",
+           int(r), (long long)K, (long long)rows, (long long)L, (long long)row_stride, (long long)l_stride);
   return m;
 }
 
@@ -838,18 +896,19 @@ CUtensorMap make_store_map(const void* base, int64_t N, int64_t rows, int64_t L,
   CUresult r = tensor_map_encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
                                       box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                                       CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (store) failed (", int(r), "): N=", N, " rows=", rows,
-              " L=", L, " row_stride=", row_stride, " l_stride=", l_stride);
+  PD_CHECK(r == CUDA_SUCCESS,
+           "cuTensorMapEncodeTiled (store) failed (%d): N=%lld rows=%lld L=%lld row_stride=%lld l_stride=%lld",
+           int(r), (long long)N, (long long)rows, (long long)L, (long long)row_stride, (long long)l_stride);
   return m;
 }
 
 // [L, rows, K] view (L may be 1): unit stride on K, 16-byte aligned rows.
 void check_operand(const at::Tensor& t, const char* name) {
-  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, ": bf16 CUDA tensor required");
-  TORCH_CHECK(t.dim() == 3 && t.stride(2) == 1, name, ": [L, rows, K] with unit stride on K required");
-  TORCH_CHECK(t.stride(1) % 8 == 0 && (t.size(0) == 1 || t.stride(0) % 8 == 0) &&
-              reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, ": rows must be 16-byte aligned");
-  TORCH_CHECK(t.size(2) % 8 == 0, name, ": K must be a multiple of 8");
+  PD_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, "%s: bf16 CUDA tensor required", name);
+  PD_CHECK(t.dim() == 3 && t.stride(2) == 1, "%s: [L, rows, K] with unit stride on K required", name);
+  PD_CHECK(t.stride(1) % 8 == 0 && (t.size(0) == 1 || t.stride(0) % 8 == 0) &&
+              reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, "%s: rows must be 16-byte aligned", name);
+  PD_CHECK(t.size(2) % 8 == 0, "%s: K must be a multiple of 8", name);
   check_extent(t, name);
 }
 
@@ -874,9 +933,10 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tcm
 // C[l, m, :N] = epi(A[l] @ B[l]^T).  A: [L, M, K], B: [L or 1, N, K] -- or, with b_kn,
 // [L or 1, K, N] (a weight used transposed, read MN-major) -- C/R/AUX: [L, M, N] views
 // (unit column stride).  epi: 0 none, 1 gelu (aux = pre-activation, optional), 2 residual (R),
-// 3 dgelu (R = pre-activation), 4 gelu storing gelu' in AUX, 5 product with R.
+// 3 dgelu (R = pre-activation), 4 gelu storing gelu' in AUX, 5 product with R, 6 relu (R = bias
+// addend), 7 acc where R > 0, 8 R * acc + R2 (AUX: acc, optional).
 void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optional<at::Tensor> R,
-             c10::optional<at::Tensor> AUX, at::Tensor err, bool b_kn) {
+             c10::optional<at::Tensor> AUX, at::Tensor err, bool b_kn, c10::optional<at::Tensor> R2) {
   check_operand(A, "A");
   check_operand(B, "B");
   const int64_t L = A.size(0), M = A.size(1), K = A.size(2), N = b_kn ? B.size(2) : B.size(1);
@@ -896,9 +956,19 @@ void tc_gemm(at::Tensor A, at::Tensor B, at::Tensor C, int64_t epi, c10::optiona
   p.C = reinterpret_cast<__nv_bfloat16*>(C.data_ptr()); p.c_ls = C.stride(0); p.c_ms = C.stride(1);
   p.epi = int(epi);
   p.err = err.data_ptr<int>();
-  TORCH_CHECK(epi >= tc::kNone && epi <= tc::kMul, "unknown epilogue ", epi);
-  TORCH_CHECK(!(epi == tc::kResidual || epi == tc::kDGelu || epi == tc::kMul) || (R && R->defined()),
+  PD_CHECK(epi >= tc::kNone && epi <= tc::kMulAdd, "unknown epilogue %lld", (long long)epi);
+  TORCH_CHECK(!(epi == tc::kResidual || epi == tc::kDGelu || epi == tc::kMul || epi == tc::kMaskPos ||
+                epi == tc::kMulAdd) || (R && R->defined()),
               "this epilogue needs R");
+  TORCH_CHECK(epi != tc::kMulAdd || (R2 && R2->defined()), "the multiply-add epilogue needs R2");
+  if (epi == tc::kMulAdd) {
+    TORCH_CHECK(R2->dim() == 3 && R2->sizes() == C.sizes() && R2->stride(2) == 1 && R2->stride(1) % 8 == 0 &&
+                (R2->size(0) == 1 || R2->stride(0) % 8 == 0) && reinterpret_cast<uintptr_t>(R2->data_ptr()) % 16 == 0 &&
+                R2->scalar_type() == at::kBFloat16, "R2 must match C (bf16, 16-byte aligned rows)");
+    check_extent(*R2, "R2");
+    p.R2 = reinterpret_cast<const __nv_bfloat16*>(R2->data_ptr()); p.r2_ls = R2->stride(0); p.r2_ms = R2->stride(1);
+    TORCH_CHECK(R->stride(1) != 0 && (L == 1 || R->stride(0) != 0), "the multiply-add factor R must be a full matrix");
+  }
   TORCH_CHECK(epi != tc::kGeluD || (AUX && AUX->defined()), "the GELU-derivative epilogue needs AUX");
   if (R && R->defined()) {
     // R: [L, M, N] view (stride 0 allowed on L and M: a bias or per-row-block addend)
