@@ -150,7 +150,14 @@ def main() -> None:
     cfg = Config.load(args.config)
     cfg.train.batch_size = args.per_gpu_batch * world
     model_desc = MODEL_DESC
-    if os.path.abspath(args.config) != os.path.abspath(CONFIG):
+    seq_len = cfg.sequence_length_total() + cfg.model.transformer.n_ns_tokens
+    if cfg.model.model_type == "dlrm":
+        mc = cfg.model
+        model_desc = (f"{os.path.splitext(os.path.basename(args.config))[0]}: DLRM {mc.dlrm_layout} "
+                      f"{len(mc.embedding_tables)} tables E{mc.embedding_dim}, bottom {mc.bottom_mlp_dims}, "
+                      f"{mc.interaction_type} x{mc.dcn_num_cross_layers} rank {mc.dcn_low_rank}, top {mc.top_mlp_dims}")
+        seq_len = 1
+    elif os.path.abspath(args.config) != os.path.abspath(CONFIG):
         ot = cfg.model.transformer
         model_desc = (f"{os.path.splitext(os.path.basename(args.config))[0]}: {ot.n_layers}L d{ot.d_model} "
                       f"{ot.n_heads}hx{ot.d_model // ot.n_heads} NS{ot.n_ns_tokens} L_S{cfg.sequence_length_total()} "
@@ -243,7 +250,7 @@ def main() -> None:
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded Zipf ids, random-init weights)",
             "impl": args.impl,
-            "config": {"model": model_desc, "global_batch": gb, "seq_len": cfg.sequence_length_total() + 16,
+            "config": {"model": model_desc, "global_batch": gb, "seq_len": seq_len,
                        "parallelism": f"dp{world}" + (" + row-wise sharded tables" if world > 1 else ""),
                        "l2": "no flush: inputs exceed L2 (GB-scale tables, >10 GB activations per step)",
                        "embedding_optimizer": cfg.train.embedding_optimizer},

@@ -21,6 +21,7 @@ from primus_dlrm_b200.models.embedding import Embeddings
 from primus_dlrm_b200.models.heads import fused_heads_loss
 from primus_dlrm_b200.models.interaction import build_interaction, make_mlp
 from primus_dlrm_b200.ops.embedding import SparseOptimizer
+from primus_dlrm_b200.ops.mlp import mlp_chain
 
 
 class DLRMBaseline(BaseModel):
@@ -75,6 +76,20 @@ class DLRMBaseline(BaseModel):
                                     for t in self.tasks})
 
     # ------------------------------------------------------------------
+    def get_num_flops_per_sample(self) -> float:
+        """Analytic fwd+bwd FLOPs per sample: 6 per multiply-accumulate of every
+        dense projection (Linear layers, the DCNv2 cross factors); lookups and
+        elementwise work are not counted (as in the OneTrans estimator)."""
+        fl = 0
+        for name, m in self.named_modules():
+            if isinstance(m, nn.Linear) and not name.startswith("emb"):
+                fl += 6 * m.in_features * m.out_features
+        inter = self.interaction
+        for attr in ("cross_u", "cross_v", "cross_weights"):
+            for p in getattr(inter, attr, []):
+                fl += 6 * p.numel()
+        return float(fl)
+
     def _dtype(self) -> torch.dtype:
         return torch.bfloat16 if (torch.is_autocast_enabled("cuda") or torch.is_autocast_enabled("cpu")) \
             else torch.float32
@@ -97,17 +112,19 @@ class DLRMBaseline(BaseModel):
         embs = self._embs(batch)
         if self.layout == "criteo":
             dense = torch.cat([batch[df.name].float() for df in fc.dense_features], dim=-1)
-            bottom = self.bottom_mlp(dense)
+            if torch.is_autocast_enabled("cuda") and dense.is_cuda:
+                dense = dense.to(torch.bfloat16)
+            bottom = mlp_chain(self.bottom_mlp, dense)
             return [bottom], [embs[f] for f in fc.scalar_feature_names]
         up = [embs[s.name] for s in fc.user_scalar_features]
         for feats in fc.sequence_groups.values():
             up.extend(embs[f] for f in feats)
         up.extend(batch[df.name] for df in fc.dense_features if not df.project and df.in_user_tower())
-        user = self.user_bottom_mlp(torch.cat([p.to(up[0].dtype) for p in up], dim=-1))
+        user = mlp_chain(self.user_bottom_mlp, torch.cat([p.to(up[0].dtype) for p in up], dim=-1))
         ip = [embs[s.name] for s in fc.item_scalar_features]
         ip.extend(self.dense_projs[df.name](batch[df.name]) for df in fc.dense_features if df.project)
         ip.extend(batch[df.name] for df in fc.dense_features if not df.project and df.in_item_tower())
-        item = self.item_bottom_mlp(torch.cat([p.to(ip[0].dtype) for p in ip], dim=-1))
+        item = mlp_chain(self.item_bottom_mlp, torch.cat([p.to(ip[0].dtype) for p in ip], dim=-1))
         items = [item]
         for df in fc.dense_features:
             if df.project and df.activation == "relu":

@@ -7,11 +7,17 @@
   deep MLP in parallel and a combining Linear.  ``low_rank > 0`` factors
   ``W = U V^T`` (rank r), the form the BASELINE DLRM-DCNv2 config uses
   (rank 512); ``low_rank = 0`` is the reference's full-rank cross.
+
+On CUDA in bf16 the MLPs and the low-rank cross layers run on the tcgen05
+GEMM (``primus_dlrm_b200.ops.mlp``): bias + ReLU in the GEMM epilogues and the
+cross layer's ``x0 * (...) + x_l`` fused into its second GEMM.
 """
 from __future__ import annotations
 
 import torch
 import torch.nn as nn
+
+from primus_dlrm_b200.ops import mlp as native_mlp
 
 
 def make_mlp(dims: list[int], dropout: float = 0.1, final_activation: bool = True) -> nn.Sequential:
@@ -42,7 +48,7 @@ class ConcatMLP(InteractionModule):
         self.output_dim = hidden_dims[-1]
 
     def forward(self, user_features, item_features):
-        return self.mlp(torch.cat(list(user_features) + list(item_features), dim=-1))
+        return native_mlp.mlp_chain(self.mlp, torch.cat(list(user_features) + list(item_features), dim=-1))
 
 
 class DotInteraction(InteractionModule):
@@ -62,7 +68,7 @@ class DotInteraction(InteractionModule):
         st = torch.stack(feats, dim=1)
         dots = torch.bmm(st, st.transpose(1, 2))
         pair = dots[:, self._iu[0], self._iu[1]]
-        return self.top_mlp(torch.cat([pair, torch.cat(feats, dim=-1)], dim=-1))
+        return native_mlp.mlp_chain(self.top_mlp, torch.cat([pair, torch.cat(feats, dim=-1)], dim=-1))
 
 
 class DCNv2(InteractionModule):
@@ -87,6 +93,10 @@ class DCNv2(InteractionModule):
 
     def cross(self, x0: torch.Tensor) -> torch.Tensor:
         xl = x0
+        if self.low_rank > 0 and native_mlp.cross_ok(x0, x0.shape[-1], self.low_rank):
+            for i in range(self.num_cross_layers):
+                xl = native_mlp.cross_layer(x0, xl, self.cross_u[i], self.cross_v[i], self.cross_biases[i])
+            return xl
         for i in range(self.num_cross_layers):
             if self.low_rank > 0:
                 proj = (xl @ self.cross_u[i].to(xl.dtype)) @ self.cross_v[i].to(xl.dtype)
@@ -97,7 +107,8 @@ class DCNv2(InteractionModule):
 
     def forward(self, user_features, item_features):
         x0 = torch.cat(list(user_features) + list(item_features), dim=-1)
-        return self.combine(torch.cat([self.cross(x0), self.deep_mlp(x0)], dim=-1))
+        h = torch.cat([self.cross(x0), native_mlp.mlp_chain(self.deep_mlp, x0)], dim=-1)
+        return native_mlp.linear(self.combine, h)
 
 
 def build_interaction(interaction_type: str, user_dims: list[int], item_dims: list[int],

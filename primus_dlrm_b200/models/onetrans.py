@@ -86,7 +86,7 @@ class MixedAttention(nn.Module):
         if x.is_cuda and self.attention_impl in ("fav4", "fav2", "turbo", "native") and no_drop \
                 and _fmha_native_ok(qkv):
             o = pyramid_attention_qkv(qkv, q_len)
-            return self.out_proj(o.reshape(B, q_len, D))
+            return dense.linear(self.out_proj, o.reshape(B, q_len, D))
         if x.is_cuda and self.attention_impl in ("fav4", "fav2", "turbo", "native") and \
                 not (self.training and self.attn_drop > 0 and self.attention_impl != "fav4"):
             o = causal_attention_all_rows(qkv, self.n_heads).reshape(B, T, D)
@@ -277,7 +277,7 @@ class OneTransModel(BaseModel):
         parts = [scal]
         for df in self.config.feature.dense_features:
             x = batch[df.name]
-            parts.append(self.dense_projs[df.name](x) if df.name in self.dense_projs else x.to(scal.dtype))
+            parts.append(self._dense_proj(df, x, scal.dtype) if df.name in self.dense_projs else x.to(scal.dtype))
         ns_raw = torch.cat([p.to(scal.dtype) for p in parts], dim=-1)
         ns_tokens = self.ns_tokenizer(ns_raw)
         # one concatenation of every S pool's tokens and the NS tokens
@@ -291,8 +291,15 @@ class OneTransModel(BaseModel):
             x = block(x, q_len=q_len, n_s_tokens=x.shape[1] - L_NS)
         x = self.final_norm(x)
         s_repr = x[:, : x.shape[1] - L_NS].float().mean(dim=1)
-        h = self.head_proj(x[:, -L_NS:].reshape(B, -1))
+        hp = self.head_proj
+        h = hp[2](dense.linear(hp[0], x[:, -L_NS:].reshape(B, -1), act="gelu"))
         return h, s_repr, scal
+
+    def _dense_proj(self, df, x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+        """Linear + activation of a projected dense feature (GEMM epilogue on CUDA)."""
+        seq = self.dense_projs[df.name]
+        act = "relu" if isinstance(seq[1], nn.ReLU) else "gelu"
+        return dense.linear(seq[0], x.to(dtype), act=act)
 
     def forward(self, batch: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
         h, _, _ = self._backbone(batch)

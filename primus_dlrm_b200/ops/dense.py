@@ -37,7 +37,10 @@ def _cast_w(w: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
 
 # gelu_d: GELU with its derivative stored in AUX; mul: acc * R (the backward
 # through that stored derivative)
-_EPI = {"": 0, None: 0, "gelu": 1, "residual": 2, "dgelu": 3, "gelu_d": 4, "mul": 5}
+# relu: bias (R) + ReLU; mask_pos: acc where R > 0 (a ReLU layer's backward);
+# mul_add: R * acc + R2 (the DCNv2 cross layer)
+_EPI = {"": 0, None: 0, "gelu": 1, "residual": 2, "dgelu": 3, "gelu_d": 4, "mul": 5, "relu": 6, "mask_pos": 7,
+        "mul_add": 8}
 _err_words: dict = {}
 
 
@@ -56,12 +59,13 @@ def gemm_error_code(device) -> int:
 
 
 def tc_gemm(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, epi: str | None = None,
-            R: torch.Tensor | None = None, AUX: torch.Tensor | None = None, b_kn: bool = False) -> torch.Tensor:
+            R: torch.Tensor | None = None, AUX: torch.Tensor | None = None, b_kn: bool = False,
+            R2: torch.Tensor | None = None) -> torch.Tensor:
     """C[l] = epi(A[l] @ B[l]^T) on the sm_100a tcgen05 kernel; A [L, M, K],
     B [L or 1, N, K] -- or with ``b_kn`` [L or 1, K, N], a weight used
-    transposed, read in place -- C/R/AUX [L, M, N] (bf16 views, unit stride on
-    the last dim)."""
-    _ext.gemm().tc_gemm(A, B, C, _EPI[epi], R, AUX, _err(A.device), b_kn)
+    transposed, read in place -- C/R/AUX/R2 [L, M, N] (bf16 views, unit stride
+    on the last dim)."""
+    _ext.gemm().tc_gemm(A, B, C, _EPI[epi], R, AUX, _err(A.device), b_kn, R2)
     return C
 
 
@@ -76,13 +80,13 @@ def tc_wgrad(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, l_sum: bool = Fa
 
 
 def _wgrad_ok(t: torch.Tensor, M: int, N: int) -> bool:
-    """Weight gradients on the tcgen05 split-K kernel (opt-in: PD_WGRAD_TC=1).
-    These products stream dY and X once and are bound by HBM; the kernel
-    measures within 1-6 % of cuBLAS's split-K GEMMs on the v6 shapes, so cuBLAS
-    stays the default."""
+    """Weight gradients on the tcgen05 split-K kernel (default; PD_WGRAD_TC=0
+    selects cuBLAS). These products stream dY and X once and are bound by HBM;
+    the kernel measures within 1-6 % of cuBLAS's split-K GEMMs on the v6 shapes
+    and writes fp32 straight from its accumulators."""
     g = _ext.gemm()
     return (hasattr(g, "tc_wgrad") and t.dtype == torch.bfloat16 and M % 64 == 0 and N % 64 == 0
-            and os.environ.get("PD_WGRAD_TC", "0") == "1")
+            and os.environ.get("PD_WGRAD_TC", "1") != "0")
 
 
 def _tc_ok(x: torch.Tensor, K: int, N: int) -> bool:
@@ -110,7 +114,10 @@ def _dw(dy, x, n_s, wdt):
     B, T, N = dy.shape
     K = x.shape[-1]
     if _wgrad_ok(dy, N, K):
-        # tcgen05, both operands as stored, split over the rows, fp32 out
+        # tcgen05, both operands as stored, split over the rows, fp32 out: the
+        # S weight over every row as one flat product (one long split-K; the
+        # S rows alone are 2048 short strided batches, which measured slower),
+        # minus the NS rows' part, each NS weight over its token's rows
         dws = tc_wgrad(dy.reshape(1, -1, N), x.reshape(1, -1, K), torch.zeros(1, N, K, device=dy.device))[0]
         if T > n_s:
             dwn = tc_wgrad(dy[:, n_s:].transpose(0, 1), x[:, n_s:].transpose(0, 1),
@@ -265,6 +272,76 @@ def mixed_linear(x: torch.Tensor, n_s: int, w_s: torch.Tensor, w_ns: torch.Tenso
     return y
 
 
+class _LinearNative(torch.autograd.Function):
+    """y = act(x W^T + b) on the tcgen05 GEMM, act in {none, gelu, relu}: the
+    bias and activation in the epilogue (GELU' stored for the backward), the
+    weight gradient on the split-K kernel. x [..., K] (K padded to a multiple
+    of 64 inside, so the data gradient's GEMM runs on the same kernel), W [N, K]
+    with N a multiple of 64."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, act: str):
+        K, N = w.shape[1], w.shape[0]
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, K).to(torch.bfloat16)
+        wb = w.to(torch.bfloat16)
+        if K % 64:
+            x2 = F.pad(x2, (0, -K % 64))
+            wb = F.pad(wb, (0, -K % 64))
+        x2, wb = x2.contiguous(), wb.contiguous()
+        M = x2.shape[0]
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+        r = b.to(torch.bfloat16).reshape(1, 1, N).expand(1, M, N) if b is not None else None
+        aux = torch.empty_like(y) if act == "gelu" else None
+        epi = {"gelu": "gelu_d", "relu": "relu"}.get(act, "residual" if r is not None else None)
+        tc_gemm(x2.reshape(1, M, -1), wb.reshape(1, N, -1), y.reshape(1, M, N), epi, R=r,
+                AUX=aux.reshape(1, M, N) if aux is not None else None)
+        ctx.save_for_backward(x2, wb, aux if act == "gelu" else (y if act == "relu" else y.new_empty(0)))
+        ctx.meta = (act, K, lead, w.dtype, b.dtype if b is not None else None)
+        return y.reshape(*lead, N)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, wb, saved = ctx.saved_tensors
+        act, K, lead, wdt, bdt = ctx.meta
+        N = wb.shape[0]
+        d = dy.reshape(-1, N).to(torch.bfloat16).contiguous()
+        if act == "gelu":
+            d = d * saved
+        elif act == "relu":
+            d = torch.where(saved > 0, d, torch.zeros((), dtype=d.dtype, device=d.device))
+        M, Kp = x2.shape
+        dx = None
+        if ctx.needs_input_grad[0]:
+            if Kp % 64 == 0:
+                dx = torch.empty(M, Kp, dtype=torch.bfloat16, device=d.device)
+                tc_gemm(d.reshape(1, M, N), wb.reshape(1, N, Kp), dx.reshape(1, M, Kp), b_kn=True)
+            else:
+                dx = torch.mm(d, wb)
+            dx = dx[:, :K].reshape(*lead, K)
+        if _wgrad_ok(d, N, Kp):
+            dw = tc_wgrad(d.reshape(1, M, N), x2.reshape(1, M, Kp), torch.zeros(1, N, Kp, device=d.device))[0]
+        else:
+            dw = torch.mm(d.t(), x2, out_dtype=torch.float32)
+        dw = dw[:, :K].to(wdt)
+        db = d.sum(0, dtype=torch.float32).to(bdt) if bdt is not None else None
+        return dx, dw, db, None
+
+
+def linear(lin: nn.Linear, x: torch.Tensor, act: str | None = None) -> torch.Tensor:
+    """``act(lin(x))`` for act in {None, "gelu", "relu"}: on the tcgen05 GEMM
+    when the shapes allow (bf16 input, output width a multiple of 64), else
+    PyTorch."""
+    if _gemm_ok(x) and x.dtype == torch.bfloat16 and lin.out_features % 64 == 0 and x.shape[-1] == lin.in_features:
+        return _LinearNative.apply(x, lin.weight, lin.bias, act or "")
+    y = lin(x)
+    if act == "gelu":
+        return F.gelu(y)
+    if act == "relu":
+        return F.relu(y)
+    return y
+
+
 class _MLP2Native(torch.autograd.Function):
     """y = W2 GELU(W1 x + b1) + b2 (+ addend[l]) on the tcgen05 GEMM: the bias
     and GELU (with GELU' of the pre-activation stored for backward) fused into
@@ -326,13 +403,35 @@ class _MLP2Native(torch.autograd.Function):
         return dx, dw1, db1, dw2, db2, (dpos.to(dt_add) if has_add else None)
 
 
+class _PadCols(torch.autograd.Function):
+    """w [N, K] -> [N, K + pad] with zero columns (gradient: the first K columns)."""
+
+    @staticmethod
+    def forward(ctx, w, pad: int):
+        ctx.k = w.shape[1]
+        return F.pad(w, (0, pad))
+
+    @staticmethod
+    def backward(ctx, g):
+        return g[:, : ctx.k], None
+
+
 def mlp2(x: torch.Tensor, l1: nn.Linear, l2: nn.Linear, addend: torch.Tensor | None = None) -> torch.Tensor:
     """l2(GELU(l1(x))) (+ addend[:L] broadcast over the batch).  On the
     tcgen05 GEMM when the shapes allow (bf16, K % 8, hidden / output % 64)."""
-    if (x.dim() == 3 and _gemm_ok(x) and x.dtype == torch.bfloat16 and l1.bias is not None
-            and l2.bias is not None and _tc_ok(x, l1.in_features, l1.out_features)
-            and l2.out_features % 64 == 0 and l1.out_features % 8 == 0):
-        return _MLP2Native.apply(x, l1.weight, l1.bias, l2.weight, l2.bias, addend)
+    if (x.dim() in (2, 3) and _gemm_ok(x) and x.dtype == torch.bfloat16 and l1.bias is not None
+            and l2.bias is not None and l1.out_features % 64 == 0 and l2.out_features % 64 == 0
+            and x.data_ptr() % 16 == 0):
+        two_d = x.dim() == 2
+        xin = x.unsqueeze(1) if two_d else x
+        K = l1.in_features
+        w1 = l1.weight
+        if K % 64:  # pad the input features (and the weight's columns) to a multiple of 64: the
+            # data gradient's GEMM then has an output width the tcgen05 kernel takes
+            xin = F.pad(xin, (0, -K % 64))
+            w1 = _PadCols.apply(w1, -K % 64)
+        y = _MLP2Native.apply(xin, w1, l1.bias, l2.weight, l2.bias, addend)
+        return y.squeeze(1) if two_d else y
     y = l2(F.gelu(l1(x)))
     if addend is not None:
         y = y + addend.to(y.dtype)
