@@ -73,7 +73,9 @@ def score_candidates(model, user_batch: dict[str, torch.Tensor], candidate_batch
     """
     inner = getattr(model, "module", model)
     if hasattr(inner, "score_candidates"):
-        return inner.score_candidates(user_batch, candidate_batch, task, batch_size)
+        from primus_dlrm_b200.parallel.fsdp import full_params
+        with full_params(inner):          # FSDP units: the scorer reads block weights directly
+            return inner.score_candidates(user_batch, candidate_batch, task, batch_size)
     C = next(iter(candidate_batch.values())).shape[0]
     out = []
     for s in range(0, C, batch_size):

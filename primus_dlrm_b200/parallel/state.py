@@ -8,6 +8,7 @@ the result is a plain single-process state dict
 (``primus_dlrm/training/dist_trainer.py:39-63`` gathers DMP shards with a
 ``dist.reduce`` of zero-padded full tables; here row blocks are gathered
 with ``dist.gather`` in bounded chunks, so no rank ever holds W copies).
+FSDP-sharded dense parameters are gathered with ``DTensor.full_tensor``.
 
 ``load_full_state_dict`` slices a full state dict into this rank's shards.
 """
@@ -15,6 +16,8 @@ from __future__ import annotations
 
 import torch
 import torch.distributed as dist
+
+from primus_dlrm_b200.parallel.fsdp import DTensor, full_tensor, local_chunk
 
 _CHUNK_ROWS = 1 << 20
 
@@ -93,8 +96,9 @@ def full_state_dict(model, dst: int = 0, group=None, with_optimizer_state: bool 
     for k, v in inner.state_dict().items():
         t = _is_table_key(model, k)
         if t is None:
+            v = full_tensor(v.detach())              # FSDP shards: gathered on every rank
             if rank == dst:
-                out[k] = v.detach().cpu()
+                out[k] = v.cpu()
             continue
         full = _full_table(t, v.detach(), dst, rank, world, group)
         if rank == dst:
@@ -144,6 +148,9 @@ def load_full_state_dict(model, sd: dict, strict: bool = True) -> None:
             src = sd[k]
             if t is not None:
                 src = _local_slice(t, src, rank, world)
+            if isinstance(v, DTensor):                # an FSDP shard: this rank's dim-0 chunk
+                v.to_local().copy_(local_chunk(src, v).to(v.dtype))
+                continue
             v.copy_(src.to(v.dtype))
     if hasattr(inner, "emb"):
         for t in inner.emb.tables():

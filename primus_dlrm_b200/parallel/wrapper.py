@@ -9,11 +9,14 @@
 * dense parameters are broadcast from rank 0 and their gradients are
   synchronised over NVLink peer memory on CUDA (``distributed.comm: peer``):
   ``PeerGradSync`` (``ddp`` / ``dmp``: two-shot all-reduce of the flat
-  gradient arena by slice kernels) or ``PeerShardedGradSync`` (``fsdp``:
+  gradient arena by slice kernels) or ``PeerShardedGradSync`` (``zero2``:
   slice reduce-scatter, AdamW on this rank's 1/W slice, parameter
-  all-gather -- optimizer state and gradients sharded ZeRO-style). With
-  ``comm: nccl`` (and on CPU / gloo) the same strategies run as NCCL
-  collectives (``FlatGradSync`` / ``ShardedGradSync``), the baseline.
+  all-gather -- optimizer state and gradients sharded, parameters
+  replicated). With ``comm: nccl`` (and on CPU / gloo) the same strategies
+  run as NCCL collectives (``FlatGradSync`` / ``ShardedGradSync``), the
+  baseline;
+* ``fsdp`` shards the parameters themselves (``parallel.fsdp``: per-block
+  units, all-gather one block ahead, fp32 master / gradient / moment shards).
 
 ``distributed.comm`` picks the sparse exchange: ``peer`` (NVLink peer-memory
 kernels, CUDA) or ``nccl`` (collective baseline; also the CPU/gloo path).
@@ -53,8 +56,8 @@ class FlatGradSync:
 
 
 class ShardedGradSync:
-    """ZeRO-style: reduce-scatter gradients so each rank owns 1/W of them,
-    update that slice, all-gather the parameters (``fsdp`` strategy)."""
+    """ZeRO-2: reduce-scatter gradients so each rank owns 1/W of them,
+    update that slice, all-gather the parameters (``zero2`` strategy)."""
 
     sharded = True
 
@@ -257,7 +260,7 @@ class PeerGradSync(_PeerDense):
 
 
 class PeerShardedGradSync(_PeerDense):
-    """ZeRO-style sharding over peer memory (``fsdp``): gradients are
+    """ZeRO-2 sharding over peer memory (``zero2``): gradients are
     reduce-scattered by the slice kernel (each rank keeps the average of its
     slice), AdamW updates that slice, and parameters are all-gathered from
     the owners' arenas. Parameters and gradients both live in shared buffers."""
@@ -298,6 +301,21 @@ class PeerShardedGradSync(_PeerDense):
         self.params.check()
 
 
+def all_gather_slices(flat: torch.Tensor, group=None) -> None:
+    """Fill every rank's copy of ``flat`` from the owners of its 64-aligned
+    1/W slices (the slice layout of ``ShardedGradSync`` and ``_PeerDense``);
+    used for checkpoints of the ``zero2`` optimizer state."""
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    n = flat.numel()
+    per = (-(-n // world) + 63) // 64 * 64
+    a, b = min(rank * per, n), min(rank * per + per, n)
+    mine = torch.zeros(per, dtype=flat.dtype, device=flat.device)
+    mine[: b - a] = flat[a:b]
+    full = torch.empty(per * world, dtype=flat.dtype, device=flat.device)
+    dist.all_gather_into_tensor(full, mine, group=group)
+    flat.copy_(full[:n])
+
+
 def broadcast_dense(model: nn.Module, group=None) -> None:
     for p in model.parameters():
         if p.requires_grad:
@@ -327,12 +345,15 @@ def wrap_model(model: nn.Module, device: torch.device, config, group=None):
     model = model.to(device)
     broadcast_dense(model, group)
     peer = device.type == "cuda" and dc.comm == "peer"
-    if dc.dense_strategy not in ("fsdp", "ddp", "dmp"):
+    if dc.dense_strategy not in ("fsdp", "zero2", "ddp", "dmp"):
         raise ValueError(f"Unknown dense_strategy: {dc.dense_strategy!r}")
-    if peer:
+    if dc.dense_strategy == "fsdp":
+        from primus_dlrm_b200.parallel.fsdp import shard_dense
+        sync = shard_dense(model, device, group, torch.bfloat16 if config.train.bf16 else None)
+    elif peer:
         # sized by the flat arena the engine builds (bind() is called with it)
-        sync = _LazyPeerSync(device, group, sharded=dc.dense_strategy == "fsdp")
-    elif dc.dense_strategy == "fsdp":
+        sync = _LazyPeerSync(device, group, sharded=dc.dense_strategy == "zero2")
+    elif dc.dense_strategy == "zero2":
         sync = ShardedGradSync(group)
     else:
         sync = FlatGradSync(group)

@@ -34,13 +34,15 @@ def save_checkpoint(path: str | Path, model, epoch: int, global_step: int, engin
     """Collective when distributed (every rank must call it)."""
     path = Path(path)
     sd = full_state_dict(model, with_optimizer_state=with_resume_state)
+    # gathered on every rank (collective when the optimizer state is sharded)
+    opt_sd = engine.full_optimizer_state() if with_resume_state and engine is not None else None
     if _rank() != 0:
         return None
     sparse = sd.pop("__sparse_state__", None)
     payload = {"epoch": int(epoch), "global_step": int(global_step), "model_state_dict": sd}
     if with_resume_state:
         if engine is not None:
-            payload["optimizer_state_dict"] = engine.optimizer.state_dict()
+            payload["optimizer_state_dict"] = opt_sd
             payload["scheduler_state_dict"] = engine.scheduler.state_dict()
             sopt = getattr(engine, "sparse_opt", None)
             if sopt is not None:
@@ -75,7 +77,8 @@ def load_checkpoint(path: str | Path, model, engine=None, strict: bool = True) -
     if "sparse_optimizer_state" in ckpt:
         load_sparse_state(model, ckpt["sparse_optimizer_state"])
     if engine is not None:
-        engine.flat.rebind()
+        if engine.flat is not None:
+            engine.flat.rebind()
         if "optimizer_state_dict" in ckpt:
             engine.optimizer.load_state_dict(ckpt["optimizer_state_dict"])
         if "scheduler_state_dict" in ckpt:

@@ -44,9 +44,17 @@ class TrainEngine:
         self.device = torch.device(device)
         tc = config.train
         self.tasks = [k for k, v in tc.loss_weights.items() if v > 0]
-        self.flat = FlatParams(dense_parameters(model))
+        # fsdp: parameters are DTensor shards owned by FSDP; no flat arena
+        self.fsdp = bool(getattr(grad_sync, "fsdp", False))
+        self.flat = None if self.fsdp else FlatParams(dense_parameters(model))
         if dense_optimizer is not None:
             self.optimizer = dense_optimizer
+        elif self.fsdp:
+            if tc.dense_optimizer != "adamw":
+                raise ValueError("dense_strategy 'fsdp' supports dense_optimizer 'adamw' only")
+            from primus_dlrm_b200.parallel.fsdp import ShardedAdamW
+            self.optimizer = ShardedAdamW(dense_parameters(model), lr=tc.lr, weight_decay=tc.weight_decay,
+                                          max_grad_norm=tc.grad_clip, group=grad_sync.group)
         elif tc.dense_optimizer == "adamw":
             self.optimizer = FusedAdamW(self.flat, lr=tc.lr, weight_decay=tc.weight_decay,
                                         max_grad_norm=tc.grad_clip)
@@ -98,7 +106,7 @@ class TrainEngine:
         if self.sparse_opt is not None:
             self.sparse_opt.lr_scale = tc.sparse_warmup_value if self.global_step < tc.sparse_warmup_steps else 1.0
         self.model.train()
-        self.flat.zero_grad()
+        self._zero_grad()
         with phase("pd.forward"), torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.use_amp):
             total, task_losses = self.compute_loss(batch)
         # dense gradient sync overlapped with the backward: buckets of the flat
@@ -107,7 +115,7 @@ class TrainEngine:
         overlapped = bucketed is not None and bucketed.begin()
         with phase("pd.backward"):
             total.backward()
-        if self.grad_sync is not None:
+        if self.grad_sync is not None and not self.fsdp:
             with phase("pd.dense_sync"):
                 if not (overlapped and bucketed.finish()):
                     self.grad_sync.sync(self.flat.grad)
@@ -122,6 +130,28 @@ class TrainEngine:
         self.scheduler.step()
         self.global_step += 1
         return total.detach(), task_losses
+
+    def _zero_grad(self) -> None:
+        if self.flat is not None:
+            self.flat.zero_grad()
+        else:
+            self.optimizer.zero_grad(set_to_none=True)
+
+    def full_optimizer_state(self) -> dict:
+        """The dense optimizer state with every shard gathered (collective
+        when the state is sharded: every rank calls it)."""
+        opt = self.optimizer
+        if hasattr(opt, "full_state_dict"):
+            return opt.full_state_dict()
+        sd = opt.state_dict()
+        if getattr(self.grad_sync, "sharded", False) and isinstance(opt, FusedAdamW):
+            # zero2: each rank's moments are valid on its own slice only
+            from primus_dlrm_b200.parallel.wrapper import all_gather_slices
+            for k in ("exp_avg", "exp_avg_sq"):
+                t = getattr(opt, k).clone()
+                all_gather_slices(t, self.grad_sync.group)
+                sd[k] = t.cpu()
+        return sd
 
     def _bucketed_sync(self):
         """The peer-memory gradient sync when its per-bucket overlap with the
@@ -154,7 +184,7 @@ class TrainEngine:
         return ex.take_comm_ms() if ex is not None and hasattr(ex, "take_comm_ms") else 0.0
 
     def state_dict(self) -> dict:
-        return {"optimizer": self.optimizer.state_dict(), "scheduler": self.scheduler.state_dict(),
+        return {"optimizer": self.full_optimizer_state(), "scheduler": self.scheduler.state_dict(),
                 "global_step": self.global_step}
 
     def load_state_dict(self, sd: dict) -> None:

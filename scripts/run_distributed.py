@@ -39,7 +39,7 @@ def parse_args(argv=None):
     p = argparse.ArgumentParser(description="Distributed OneTrans / DLRM training (B200)")
     p.add_argument("--config", required=True)
     p.add_argument("--data-root", default=None)
-    p.add_argument("--dense-strategy", default="ddp", choices=["ddp", "fsdp", "dmp"])
+    p.add_argument("--dense-strategy", default="ddp", choices=["ddp", "fsdp", "zero2", "dmp"])
     p.add_argument("--embedding-sharding", default="auto",
                    choices=["auto", "table_wise", "row_wise", "data_parallel", "column_wise"])
     p.add_argument("--max-steps", type=int, default=0)

@@ -97,7 +97,7 @@ def _oracle(dense, opt, steps, world=2):
 # gradient magnitude, which amplifies summation-order rounding on rows whose
 # gradients nearly cancel: those runs get a looser table tolerance.
 @pytest.mark.parametrize("dense,opt,tab_atol", [("ddp", "sgd", 1e-6), ("ddp", "row_wise_adagrad", 5e-4),
-                                                ("fsdp", "adam", 5e-4)])
+                                                ("fsdp", "adam", 5e-4), ("zero2", "adam", 5e-4)])
 def test_sharded_training_matches_single_process(dense, opt, tab_atol):
     res = run_ranks(_dist_worker, 2, dense, opt, 2)
     ref_losses, ref_sd = _oracle(dense, opt, 2)
@@ -119,3 +119,50 @@ def test_plan_is_identical_on_every_rank():
     res = run_ranks(_plan_worker, 2)
     assert res[0] == res[1]
     assert res[0]["artist"] == ("table_wise", 1)
+
+
+def _fsdp_worker(rank, world, tmp):
+    """fsdp stores 1/W of every dense parameter and of the AdamW moments, and a
+    checkpoint saved from the shards resumes to the same next step."""
+    import torch.distributed as dist
+
+    from primus_dlrm_b200.parallel.build import build_model
+    from primus_dlrm_b200.parallel.fsdp import DTensor, ShardedAdamW
+    from primus_dlrm_b200.parallel.wrapper import wrap_model
+    from primus_dlrm_b200.training.checkpoint import load_checkpoint, save_checkpoint
+    from primus_dlrm_b200.training.engine import TrainEngine
+    cfg = _config("fsdp", "adam")
+
+    def make():
+        torch.manual_seed(0)
+        m, s = wrap_model(build_model(cfg, meta_device=True), torch.device("cpu"), cfg)
+        return m, TrainEngine(m, cfg, torch.device("cpu"), grad_sync=s)
+
+    model, eng = make()
+    assert isinstance(eng.optimizer, ShardedAdamW) and eng.flat is None
+    dense = [p for n, p in model.named_parameters() if p.requires_grad and not n.startswith("emb")]
+    assert dense and all(isinstance(p, DTensor) for p in dense)
+    local = sum(p.to_local().numel() for p in dense)
+    full = sum(p.numel() for p in dense)
+    assert local <= full / world + 64 * len(dense), (local, full)
+    assert sum(m.numel() for m in eng.optimizer.exp_avg) == local
+    B = 8
+    bs = _batches(cfg, world, 3, B)
+    loc = [{k: v[rank * B:(rank + 1) * B] for k, v in b.items()} for b in bs]
+    for b in loc[:2]:
+        eng.step(b)
+    path = os.path.join(tmp, "fsdp.pt")
+    save_checkpoint(path, model, 0, eng.global_step, engine=eng, config=cfg)
+    dist.barrier()
+    want = float(eng.step(loc[2])[0])
+    model2, eng2 = make()
+    load_checkpoint(path, model2, engine=eng2)
+    got = float(eng2.step(loc[2])[0])
+    return want, got, eng2.global_step
+
+
+def test_fsdp_shards_parameters_and_resumes(tmp_path):
+    res = run_ranks(_fsdp_worker, 2, str(tmp_path))
+    for want, got, step in res.values():
+        assert got == pytest.approx(want, rel=1e-5, abs=1e-6)
+        assert step == 3
