@@ -123,6 +123,7 @@ def main() -> None:
     ap.add_argument("--config", default=CONFIG)
     ap.add_argument("--per-gpu-batch", type=int, default=PER_GPU_BATCH)
     ap.add_argument("--comm", default=None, choices=[None, "peer", "nccl"])
+    ap.add_argument("--dense-strategy", default=None, choices=[None, "ddp", "fsdp", "zero2", "dmp"])
     args = ap.parse_args()
     if args.impl == "reference":
         _reference_arm(args)
@@ -166,6 +167,8 @@ def main() -> None:
         cfg.train.kernels = "eager"
     if args.comm:
         cfg.distributed.comm = args.comm
+    if args.dense_strategy:
+        cfg.distributed.dense_strategy = args.dense_strategy
     model, engine = build_training(cfg, device)
 
     n_batches = 3
@@ -236,10 +239,13 @@ def main() -> None:
         if obj is not None and hasattr(obj, "check"):
             obj.check()
 
-    stats = torch.tensor([ms, e2e_ms, float(launches), a2a_ms], device=device, dtype=torch.float64)
+    peak_gb = torch.cuda.max_memory_allocated(device) / 2 ** 30
+    stats = torch.tensor([ms, e2e_ms, float(launches), a2a_ms, peak_gb], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, launches, a2a_ms = stats.tolist()
+    ms, e2e_ms, launches, a2a_ms, peak_gb = stats.tolist()
+    dense = cfg.distributed.dense_strategy if world > 1 else "single"
+    par = {"ddp": "dp", "dmp": "dp", "fsdp": "fsdp", "zero2": "zero2-dp"}.get(dense, "dp")
     gb = args.per_gpu_batch * world
     if rank == 0:
         flops = model.get_num_flops_per_sample() if hasattr(model, "get_num_flops_per_sample") else 0.0
@@ -251,7 +257,7 @@ def main() -> None:
             "dtype": "bf16", "data": "synthetic (seeded Zipf ids, random-init weights)",
             "impl": args.impl,
             "config": {"model": model_desc, "global_batch": gb, "seq_len": seq_len,
-                       "parallelism": f"dp{world}" + (" + row-wise sharded tables" if world > 1 else ""),
+                       "parallelism": f"{par}{world}" + (" + row-wise sharded tables" if world > 1 else ""),
                        "l2": "no flush: inputs exceed L2 (GB-scale tables, >10 GB activations per step)",
                        "embedding_optimizer": cfg.train.embedding_optimizer},
             "e2e": {"value": round(gb / (e2e_ms / 1000.0), 1), "unit": "samples/s",
@@ -263,6 +269,7 @@ def main() -> None:
                                  "route/dedup/push/barrier/update) on the compute stream; 0 on 1 GPU"),
             "tflops_per_gpu": round(flops * args.per_gpu_batch / (ms / 1000.0) / 1e12, 1),
             "clocks": clocks,
+            "peak_mem_gib_max_rank": round(peak_gb, 2),
             **({"exchange_bwd_phase_ms_rank0": phases} if phases else {}),
         })
     if world > 1:

@@ -270,3 +270,70 @@ def test_overlapped_bucket_sync_matches_sync_after_backward():
     sd1, sd0 = res[0]["1"][1], res[0]["0"][1]
     for k in sd0:
         torch.testing.assert_close(sd1[k], sd0[k], rtol=1e-3, atol=1e-5, msg=lambda m: f"{k}: {m}")
+
+
+def _fsdp_vs_ddp(rank, world):
+    """The same bf16 steps with FSDP-sharded dense parameters and with the
+    replicated (DDP) arena: losses agree to bf16 rounding and each FSDP rank
+    holds 1/W of the dense parameters."""
+    import copy
+
+    import torch.distributed as dist
+
+    from primus_dlrm_b200.data.synthetic import generate_batch
+    from primus_dlrm_b200.parallel.build import build_model
+    from primus_dlrm_b200.parallel.fsdp import DTensor
+    from primus_dlrm_b200.parallel.state import full_state_dict, load_full_state_dict
+    from primus_dlrm_b200.parallel.wrapper import wrap_model
+    from primus_dlrm_b200.training.engine import TrainEngine
+    dev = torch.device("cuda", rank)
+    torch.manual_seed(0)
+
+    def cfg_of(dense):
+        cfg = _cfg("peer", opt="adam")
+        cfg.model.transformer.d_model = 128
+        cfg.distributed.dense_strategy = dense
+        cfg.train.bf16 = True
+        return cfg
+    init = copy.deepcopy(build_model(cfg_of("ddp")).state_dict())
+    out = {}
+    for dense in ("fsdp", "ddp"):
+        cfg = cfg_of(dense)
+        model = build_model(cfg, device=dev, meta_device=True)
+        model, sync = wrap_model(model, dev, cfg)
+        load_full_state_dict(model, init)
+        eng = TrainEngine(model, cfg, dev, grad_sync=sync)
+        losses = []
+        for s in range(4):
+            b = generate_batch(cfg, 64, seed=1000 * s + rank)
+            loss, _ = eng.step({k: v.to(dev) for k, v in b.items()})
+            losses.append(float(loss))
+        torch.cuda.synchronize()
+        ps = [p for n, p in model.named_parameters() if p.requires_grad and not n.startswith("emb")]
+        local = sum((p.to_local() if isinstance(p, DTensor) else p).numel() for p in ps)
+        sd = full_state_dict(model)
+        out[dense] = (losses, local, sum(p.numel() for p in ps),
+                      {k: v for k, v in sd.items() if not k.startswith("emb.")})
+        dist.barrier()
+        del eng, model
+    return out
+
+
+def test_fsdp_matches_ddp_and_shards_parameters():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = _world()
+    res = run_nccl(_fsdp_vs_ddp, world)
+    for r, d in res.items():
+        lf, ld = d["fsdp"][0], d["ddp"][0]
+        assert lf == pytest.approx(ld, rel=2e-2, abs=2e-2), (r, lf, ld)
+        local, full = d["fsdp"][1], d["fsdp"][2]
+        assert local < full / world * 1.1 + 4096, (local, full)
+        assert d["ddp"][1] == full
+    sf, sd = res[0]["fsdp"][3], res[0]["ddp"][3]
+    assert set(sf) == set(sd)
+    # Adam moves every weight by about lr per step whatever the gradient's
+    # size, so a bf16 rounding flip of a tiny gradient's sign can move a weight
+    # by up to 2 lr per step: 4 steps at lr 1e-3
+    for k in sd:
+        torch.testing.assert_close(sf[k].float(), sd[k].float(), rtol=0, atol=8e-3, msg=lambda m: f"{k}: {m}")
