@@ -122,28 +122,37 @@ __device__ __forceinline__ float exp2f_approx(float x) {
 }
 
 // GELU(x) = x * Phi(x) (the exact, erf-based form used by nn.GELU()).
-// erf is evaluated with Abramowitz & Stegun, Handbook of Mathematical
-// Functions (1964), formula 7.1.26: erf(x) = 1 - (a1 t + ... + a5 t^5) e^{-x^2},
-// t = 1 / (1 + p x), |error| <= 1.5e-7 -- far below bf16 resolution.  The same
-// exponential gives the Gaussian density for GELU's derivative, so one
-// reciprocal and one exponential cover both.
+// Normal CDF with no division and no exponential, so the GELU epilogues do
+// not queue on the MUFU pipe: Phi(x) = 1/2 + x R(t), t = 2 x^2 / c^2 - 1,
+// x clamped to [-c, c], c = 4.5. R is a degree-9 polynomial in t: the
+// L-infinity fit of the absolute error of x R(t) to Phi(x) - 1/2 on [0, c],
+// computed by Lawson's iteratively reweighted least squares
+// (csrc/gen_gelu_poly.py prints the coefficients and the error). Max |error|
+// over all x in fp32: 3.7e-6 (beyond the clamp the tail 1 - Phi(c) = 3.4e-6 is dropped).
+__device__ __forceinline__ float norm_cdf_poly(float x) {
+  const float xc = fminf(fmaxf(x, -4.5f), 4.5f);
+  const float t = fmaf(xc * xc, 0.0987654328f, -1.0f);
+  float r = fmaf(-0.00193071156f, t, 0.00496269623f);
+  r = fmaf(r, t, -0.00606983015f);
+  r = fmaf(r, t, 0.00965323579f);
+  r = fmaf(r, t, -0.0184842162f);
+  r = fmaf(r, t, 0.0288576446f);
+  r = fmaf(r, t, -0.0402369164f);
+  r = fmaf(r, t, 0.0546374917f);
+  r = fmaf(r, t, -0.0771858841f);
+  r = fmaf(r, t, 0.156906039f);
+  const float p = fmaf(xc, r, 0.5f);
+  // beyond the clamp the tail is dropped (exactly 0 or 1), so GELU(x) -> 0 for x -> -inf
+  return fabsf(x) < 4.5f ? p : (x > 0.f ? 1.f : 0.f);
+}
+
 struct GeluEval { float cdf, pdf; };
 __device__ __forceinline__ GeluEval gelu_eval(float x) {
-  // z = |x| / sqrt(2); p z and -z^2 are formed from |x| with the constants folded
-  const float ax = fabsf(x);
-  const float t = __fdividef(1.0f, fmaf(0.23164188826636045f, ax, 1.0f));   // 1 / (1 + p z)
-  // (a1 t + ... + a5 t^5) / 2: the A&S coefficients halved (exact in binary)
-  float poly = fmaf(0.5307027145f, t, -0.7265760135f);
-  poly = fmaf(poly, t, 0.7107068705f);
-  poly = fmaf(poly, t, -0.142248368f);
-  poly = fmaf(poly, t, 0.127414796f);
-  poly *= t;
-  const float e = exp2f_approx(ax * ax * -0.72134752044448170f);          // exp(-x^2 / 2)
-  const float half_erf = fmaf(-poly, e, 0.5f);                              // erf(|x| / sqrt 2) / 2
-  const float cdf = 0.5f + copysignf(half_erf, x);                          // Phi(x)
-  return GeluEval{cdf, 0.3989422804014327f * e};                            // Phi(x), phi(x)
+  // phi(x) = exp(-x^2 / 2) / sqrt(2 pi): one MUFU exponential, needed by GELU' only
+  const float e = exp2f_approx(x * x * -0.72134752044448170f);
+  return GeluEval{norm_cdf_poly(x), 0.3989422804014327f * e};
 }
-__device__ __forceinline__ float gelu_f(float x) { return x * gelu_eval(x).cdf; }
+__device__ __forceinline__ float gelu_f(float x) { return x * norm_cdf_poly(x); }
 __device__ __forceinline__ float gelu_grad_f(float x) {
   const GeluEval g = gelu_eval(x);
   return g.cdf + x * g.pdf;

@@ -44,7 +44,7 @@ constexpr int kEpiWarps = 12;  // three warps per TMEM lane quarter, splitting t
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-// kGeluD: C = GELU(x), AUX = GELU'(x) for x = bf16(acc + R) -- the derivative
+// kGeluD: C = GELU(x), AUX = GELU'(x) for x = acc + R in fp32 -- the derivative
 // stored in the forward makes the backward's epilogue a plain product (kMul:
 // C = acc * R), with no transcendental per element.
 // kRelu: C = max(acc + R, 0) (R: a bias through a zero row stride);
@@ -482,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             float d[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const float x = __bfloat162float(__float2bfloat16_rn(v[8 * j + e]));
+              const float x = v[8 * j + e];      // the fp32 pre-activation (no bf16 round trip)
               const GeluEval g = gelu_eval(x);
               v[8 * j + e] = x * g.cdf;
               d[e] = fmaf(x, g.pdf, g.cdf);

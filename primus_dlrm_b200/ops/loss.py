@@ -18,8 +18,10 @@ class _HeadsLossFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, W, b, labels, task_weights, regression):
         C = _ext.core()
-        out, logits, dlogit = C.heads_loss_fwd(h.contiguous(), W.contiguous(), b.contiguous(),
-                                               labels.contiguous(), task_weights, regression)
+        # the kernel keeps the head weights in fp32 (FSDP may hand them over in bf16)
+        ctx.wdt, ctx.bdt = W.dtype, b.dtype
+        W, b = W.float().contiguous(), b.float().contiguous()
+        out, logits, dlogit = C.heads_loss_fwd(h.contiguous(), W, b, labels.contiguous(), task_weights, regression)
         ctx.save_for_backward(h, W, dlogit)
         total = out[0]
         per_task = out[1:]
@@ -33,7 +35,7 @@ class _HeadsLossFn(torch.autograd.Function):
         if g_total is None:
             g_total = torch.zeros((), device=h.device)
         dh, dW, db = C.heads_loss_bwd(h.contiguous(), W.contiguous(), dlogit, g_total.reshape(1))
-        return dh, dW, db, None, None, None
+        return dh, dW.to(ctx.wdt), db.to(ctx.bdt), None, None, None
 
 
 def heads_loss_ref(h, W, b, labels, task_weights, regression):

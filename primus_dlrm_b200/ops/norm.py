@@ -19,6 +19,12 @@ def _rows_ok(t: torch.Tensor) -> bool:
             and t.data_ptr() % 16 == 0 and t.stride(0) % 8 == 0) or t.is_contiguous()
 
 
+def _f32(t: torch.Tensor | None) -> torch.Tensor | None:
+    """Norm parameters as the kernels take them: contiguous fp32 (FSDP may hand
+    them over in bf16; the gradient is cast back to the parameter's dtype)."""
+    return t if t is None or (t.dtype == torch.float32 and t.is_contiguous()) else t.float().contiguous()
+
+
 def _use_native(x: torch.Tensor) -> bool:
     return x.is_cuda and x.dtype == torch.bfloat16 and _ext.native_enabled(x.device) \
         and x.shape[-1] % 8 == 0 and x.shape[-1] <= 2048
@@ -30,6 +36,8 @@ class _NormFn(torch.autograd.Function):
         C = _ext.core()
         xc = x if _rows_ok(x) else x.contiguous()
         rc = (res if _rows_ok(res) else res.contiguous()) if res is not None else None
+        ctx.pdt = (weight.dtype, bias.dtype if bias is not None else None)
+        weight, bias = _f32(weight), _f32(bias)
         y, z, rstd, mean = C.norm_fwd(xc, rc, weight, bias, eps, kind)
         xin = z if res is not None else xc
         if res is None and not xin.is_contiguous():
@@ -54,7 +62,8 @@ class _NormFn(torch.autograd.Function):
             dy = torch.zeros_like(xin)
         dx, dw, db = C.norm_bwd(xin, dy.to(torch.bfloat16), dz.to(torch.bfloat16) if dz is not None else None,
                                 weight, rstd, mean if ctx.kind == 1 else None, ctx.kind)
-        return (dx, dx if ctx.fused else None, dw, db if ctx.has_bias else None, None, None)
+        dw, db = dw.to(ctx.pdt[0]), (db.to(ctx.pdt[1]) if ctx.has_bias else None)
+        return (dx, dx if ctx.fused else None, dw, db, None, None)
 
 
 class _NormTailFn(torch.autograd.Function):
@@ -68,6 +77,8 @@ class _NormTailFn(torch.autograd.Function):
     def forward(ctx, x, weight, bias, eps: float, kind: int, q_len: int):
         C = _ext.core()
         xc = x if x.is_contiguous() else x.contiguous()
+        ctx.pdt = (weight.dtype, bias.dtype if bias is not None else None)
+        weight, bias = _f32(weight), _f32(bias)
         y, _, rstd, mean = C.norm_fwd(xc, None, weight, bias, eps, kind)
         T = x.shape[1]
         ctx.kind, ctx.has_bias, ctx.off = kind, bias is not None, T - q_len
@@ -83,7 +94,7 @@ class _NormTailFn(torch.autograd.Function):
         ex = dtail.to(torch.bfloat16) if dtail is not None else None
         dx, dw, db = C.norm_bwd(xin, dy.to(torch.bfloat16), ex, weight, rstd,
                                 mean if ctx.kind == 1 else None, ctx.kind, ctx.off if ex is not None else 0)
-        return dx, dw, db if ctx.has_bias else None, None, None, None
+        return dx, dw.to(ctx.pdt[0]), (db.to(ctx.pdt[1]) if ctx.has_bias else None), None, None, None
 
 
 def norm_with_tail(norm: nn.Module, x: torch.Tensor, q_len: int) -> tuple[torch.Tensor, torch.Tensor]:
