@@ -123,39 +123,95 @@ __device__ __forceinline__ float exp2f_approx(float x) {
 
 // GELU(x) = x * Phi(x) (the exact, erf-based form used by nn.GELU()).
 // Normal CDF with no division and no exponential, so the GELU epilogues do
-// not queue on the MUFU pipe: Phi(x) = 1/2 + x R(t), t = 2 x^2 / c^2 - 1,
-// x clamped to [-c, c], c = 4.5. R is a degree-9 polynomial in t: the
-// L-infinity fit of the absolute error of x R(t) to Phi(x) - 1/2 on [0, c],
-// computed by Lawson's iteratively reweighted least squares
-// (csrc/gen_gelu_poly.py prints the coefficients and the error). Max |error|
-// over all x in fp32: 3.7e-6 (beyond the clamp the tail 1 - Phi(c) = 3.4e-6 is dropped).
+// not queue on the MUFU pipe:
+//   Phi(x) = sat(1/2 + x R(t)),  t = min(2 x^2 / c^2 - 1, 1),  c = 4.5,
+// sat clamping to [0, 1]. R is a degree-9 polynomial in t: the L-infinity fit
+// of the absolute error of x R(t) to Phi(x) - 1/2 on [0, c] by Lawson's
+// iteratively reweighted least squares, under the constraint c R(1) =
+// 1/2 + 2e-6 -- so for |x| >= c (t held at 1) the saturation returns exactly 0
+// or 1 (csrc/gen_gelu_poly.py prints the coefficients and the error). Max
+// |error| over all x in fp32: 5.5e-6.
+#define PD_CDF_T_SCALE 0.0987654328f
+#define PD_CDF_HORNER(R, T, FMA, K)                                              \
+  R = FMA(K(-0.00155825319f), T, K(0.00492038578f));                           \
+  R = FMA(R, T, K(-0.00684563117f));                                             \
+  R = FMA(R, T, K(0.00971821137f));                                              \
+  R = FMA(R, T, K(-0.0179516189f));                                              \
+  R = FMA(R, T, K(0.0288285892f));                                               \
+  R = FMA(R, T, K(-0.0403702296f));                                              \
+  R = FMA(R, T, K(0.0546411946f));                                               \
+  R = FMA(R, T, K(-0.0771770775f));                                              \
+  R = FMA(R, T, K(0.156905979f))
+#define PD_ID(v) (v)
+
 __device__ __forceinline__ float norm_cdf_poly(float x) {
-  const float xc = fminf(fmaxf(x, -4.5f), 4.5f);
-  const float t = fmaf(xc * xc, 0.0987654328f, -1.0f);
-  float r = fmaf(-0.00193071156f, t, 0.00496269623f);
-  r = fmaf(r, t, -0.00606983015f);
-  r = fmaf(r, t, 0.00965323579f);
-  r = fmaf(r, t, -0.0184842162f);
-  r = fmaf(r, t, 0.0288576446f);
-  r = fmaf(r, t, -0.0402369164f);
-  r = fmaf(r, t, 0.0546374917f);
-  r = fmaf(r, t, -0.0771858841f);
-  r = fmaf(r, t, 0.156906039f);
-  const float p = fmaf(xc, r, 0.5f);
-  // beyond the clamp the tail is dropped (exactly 0 or 1), so GELU(x) -> 0 for x -> -inf
-  return fabsf(x) < 4.5f ? p : (x > 0.f ? 1.f : 0.f);
+  const float t = fminf(fmaf(x * x, PD_CDF_T_SCALE, -1.0f), 1.0f);
+  float r;
+  PD_CDF_HORNER(r, t, fmaf, PD_ID);
+  return __saturatef(fmaf(x, r, 0.5f));
 }
 
-struct GeluEval { float cdf, pdf; };
-__device__ __forceinline__ GeluEval gelu_eval(float x) {
-  // phi(x) = exp(-x^2 / 2) / sqrt(2 pi): one MUFU exponential, needed by GELU' only
-  const float e = exp2f_approx(x * x * -0.72134752044448170f);
-  return GeluEval{norm_cdf_poly(x), 0.3989422804014327f * e};
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two values).
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
 }
+__device__ __forceinline__ uint64_t pk2s(float v) { return pk2(v, v); }
+__device__ __forceinline__ void pk2_split(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t pk2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t pk2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// Phi of two values (same polynomial as norm_cdf_poly, Horner on pairs); u = x^2.
+__device__ __forceinline__ void norm_cdf_poly2(float x0, float x1, uint64_t u, float& p0, float& p1) {
+  float t0, t1;
+  pk2_split(pk2_fma(u, pk2s(PD_CDF_T_SCALE), pk2s(-1.0f)), t0, t1);
+  const uint64_t t = pk2(fminf(t0, 1.0f), fminf(t1, 1.0f));
+  uint64_t r;
+  PD_CDF_HORNER(r, t, pk2_fma, pk2s);
+  float r0, r1;
+  pk2_split(r, r0, r1);
+  p0 = __saturatef(fmaf(x0, r0, 0.5f));
+  p1 = __saturatef(fmaf(x1, r1, 0.5f));
+}
+
+// GELU of two values.
+__device__ __forceinline__ void gelu2(float& x0, float& x1) {
+  float p0, p1;
+  norm_cdf_poly2(x0, x1, pk2_mul(pk2(x0, x1), pk2(x0, x1)), p0, p1);
+  pk2_split(pk2_mul(pk2(x0, x1), pk2(p0, p1)), x0, x1);
+}
+
+// GELU'(x) = Phi(x) + x phi(x) of two values, phi(x) = exp(-x^2 / 2) / sqrt(2 pi)
+// (one MUFU exponential each); with_gelu also returns GELU in x0, x1.
+template <bool with_gelu>
+__device__ __forceinline__ void gelu_grad2(float& x0, float& x1, float& d0, float& d1) {
+  const uint64_t x = pk2(x0, x1);
+  const uint64_t u = pk2_mul(x, x);
+  float p0, p1;
+  norm_cdf_poly2(x0, x1, u, p0, p1);
+  float a0, a1;
+  pk2_split(pk2_mul(u, pk2s(-0.72134752044448170f)), a0, a1);               // -x^2 / (2 ln 2)
+  const uint64_t e = pk2(exp2f_approx(a0), exp2f_approx(a1));
+  const uint64_t p = pk2(p0, p1);
+  pk2_split(pk2_fma(pk2_mul(x, pk2s(0.3989422804014327f)), e, p), d0, d1);  // Phi + x phi
+  if (with_gelu) pk2_split(pk2_mul(x, p), x0, x1);
+}
+
 __device__ __forceinline__ float gelu_f(float x) { return x * norm_cdf_poly(x); }
 __device__ __forceinline__ float gelu_grad_f(float x) {
-  const GeluEval g = gelu_eval(x);
-  return g.cdf + x * g.pdf;
+  const float e = exp2f_approx(x * x * -0.72134752044448170f);
+  return fmaf(x * 0.3989422804014327f, e, norm_cdf_poly(x));
 }
 
 }  // namespace pd

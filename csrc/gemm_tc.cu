@@ -474,19 +474,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           }
         }
         if (p.epi == kGelu) {
+          // GELU of the bf16-rounded pre-activation (the value AUX stores)
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = gelu_f(__bfloat162float(__float2bfloat16_rn(v[j])));
+          for (int j = 0; j < 32; j += 2) {
+            float x0 = __bfloat162float(__float2bfloat16_rn(v[j]));
+            float x1 = __bfloat162float(__float2bfloat16_rn(v[j + 1]));
+            gelu2(x0, x1);
+            v[j] = x0;
+            v[j + 1] = x1;
+          }
         } else if (p.epi == kGeluD) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             float d[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float x = v[8 * j + e];      // the fp32 pre-activation (no bf16 round trip)
-              const GeluEval g = gelu_eval(x);
-              v[8 * j + e] = x * g.cdf;
-              d[e] = fmaf(x, g.pdf, g.cdf);
-            }
+            for (int e = 0; e < 8; e += 2)       // the fp32 pre-activation (no bf16 round trip)
+              gelu_grad2<true>(v[8 * j + e], v[8 * j + e + 1], d[e], d[e + 1]);
             uint4 pk;
             __nv_bfloat162 h0 = __floats2bfloat162_rn(d[0], d[1]);
             __nv_bfloat162 h1 = __floats2bfloat162_rn(d[2], d[3]);
@@ -563,8 +566,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 f = __bfloat1622float2(h[e]);
-              v[8 * j + 2 * e] *= gelu_grad_f(f.x);
-              v[8 * j + 2 * e + 1] *= gelu_grad_f(f.y);
+              float x0 = f.x, x1 = f.y, d0, d1;
+              gelu_grad2<false>(x0, x1, d0, d1);
+              v[8 * j + 2 * e] *= d0;
+              v[8 * j + 2 * e + 1] *= d1;
             }
           }
         }

@@ -337,3 +337,67 @@ def test_fsdp_matches_ddp_and_shards_parameters():
     # by up to 2 lr per step: 4 steps at lr 1e-3
     for k in sd:
         torch.testing.assert_close(sf[k].float(), sd[k].float(), rtol=0, atol=8e-3, msg=lambda m: f"{k}: {m}")
+
+
+def _pooled_cfg(comm):
+    from primus_dlrm_b200.config import Config, TableShardingSpec
+    cfg = Config.load(os.path.join(os.path.dirname(TINY), "dlrm_baseline.yaml"))
+    cfg.data.history_length = 12
+    cfg.model.dropout = 0.0
+    kinds = {"hist_item": "row_wise", "item": "row_wise", "hist_artist": "table_wise", "artist": "table_wise",
+             "hist_album": "row_wise", "album": "data_parallel", "uid": "row_wise"}
+    for t in cfg.model.embedding_tables:
+        t.num_embeddings = {"hist_item": 5003, "item": 5003, "hist_artist": 701, "artist": 701,
+                            "hist_album": 1301, "album": 1301, "uid": 997}[t.name]
+        t.sharding = TableShardingSpec(sharding_type=kinds[t.name], ranks=[1] if "artist" in t.name else None)
+    cfg.distributed.embedding_sharding.enabled = True
+    cfg.distributed.comm = comm
+    cfg.train.embedding_optimizer = "row_wise_adagrad"
+    cfg.train.bf16 = False
+    cfg.train.warmup_steps = 1
+    return cfg
+
+
+def _pooled_peer_vs_nccl(rank, world):
+    """DLRM two-tower (mean-pooled history bags) with the peer-memory exchange
+    against the NCCL all-to-all baseline: same losses and tables."""
+    import copy
+
+    import torch.distributed as dist
+
+    from primus_dlrm_b200.data.synthetic import generate_batch
+    from primus_dlrm_b200.parallel.build import build_model
+    from primus_dlrm_b200.parallel.state import full_state_dict, load_full_state_dict
+    from primus_dlrm_b200.parallel.wrapper import wrap_model
+    from primus_dlrm_b200.training.engine import TrainEngine
+    dev = torch.device("cuda", rank) if torch.cuda.is_available() else torch.device("cpu")
+    torch.manual_seed(0)
+    init = copy.deepcopy(build_model(_pooled_cfg("nccl")).state_dict())
+    out = {}
+    for comm in (("peer", "nccl") if dev.type == "cuda" else ("nccl",)):
+        cfg = _pooled_cfg(comm)
+        model = build_model(cfg, device=dev, meta_device=True)
+        model, sync = wrap_model(model, dev, cfg)
+        load_full_state_dict(model, init)
+        eng = TrainEngine(model, cfg, dev, grad_sync=sync)
+        assert any(model.emb.is_pooled(f) for f in cfg.feature.all_ec_feature_names())
+        losses = []
+        for s in range(3):
+            b = generate_batch(cfg, 64, seed=1000 * s + rank)
+            loss, _ = eng.step({k: v.to(dev) for k, v in b.items()})
+            losses.append(float(loss))
+        model.emb.check_errors()
+        out[comm] = (losses, full_state_dict(model))
+        dist.barrier()
+    return out
+
+
+def test_pooled_peer_exchange_matches_collective_baseline():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = run_nccl(_pooled_peer_vs_nccl, min(_world(), 2))
+    for r in res:
+        assert res[r]["peer"][0] == pytest.approx(res[r]["nccl"][0], rel=2e-3, abs=2e-3)
+    sd_p, sd_n = res[0]["peer"][1], res[0]["nccl"][1]
+    for k in sd_n:
+        torch.testing.assert_close(sd_p[k], sd_n[k], rtol=2e-3, atol=2e-4, msg=lambda m: f"{k}: {m}")
