@@ -420,9 +420,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t(a * BN);
       // one chunk: 32 accumulator columns of this warp's 32 rows, already in r
       auto process = [&](uint32_t (&r)[32], int c) -> bool {
-        // the previous chunk's TMA stores have read the staging blocks
-        if (lane == 0) bulk_wait_read_all();
-        __syncwarp();
+        // the previous chunk's TMA stores have read the staging blocks: waited
+        // for here when an R block is about to land in one of them, else only
+        // just before the first staging write (the math of this chunk overlaps
+        // the stores' shared-memory reads)
+        bool waited = false;
+        auto wait_staging = [&]() {
+          if (waited) return;
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+          waited = true;
+        };
+        if (has_r) wait_staging();
         uint8_t* stR = stR0 + (r_tma ? ((kc & 1) << 11) : 0);
         uint8_t* stX = stR;   // AUX staging reuses the R block once it has been consumed
         if (has_r) {
@@ -461,6 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           }
         }
         if (p.epi == kGelu && p.AUX) {
+          wait_staging();
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             uint4 pk;
@@ -484,20 +494,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             v[j + 1] = x1;
           }
         } else if (p.epi == kGeluD) {
+          uint4 dpk[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             float d[8];
 #pragma unroll
             for (int e = 0; e < 8; e += 2)       // the fp32 pre-activation (no bf16 round trip)
               gelu_grad2<true>(v[8 * j + e], v[8 * j + e + 1], d[e], d[e + 1]);
-            uint4 pk;
             __nv_bfloat162 h0 = __floats2bfloat162_rn(d[0], d[1]);
             __nv_bfloat162 h1 = __floats2bfloat162_rn(d[2], d[3]);
             __nv_bfloat162 h2 = __floats2bfloat162_rn(d[4], d[5]);
             __nv_bfloat162 h3 = __floats2bfloat162_rn(d[6], d[7]);
-            pk.x = *reinterpret_cast<uint32_t*>(&h0); pk.y = *reinterpret_cast<uint32_t*>(&h1);
-            pk.z = *reinterpret_cast<uint32_t*>(&h2); pk.w = *reinterpret_cast<uint32_t*>(&h3);
-            *reinterpret_cast<uint4*>(stX + sw(lane, j)) = pk;
+            dpk[j].x = *reinterpret_cast<uint32_t*>(&h0); dpk[j].y = *reinterpret_cast<uint32_t*>(&h1);
+            dpk[j].z = *reinterpret_cast<uint32_t*>(&h2); dpk[j].w = *reinterpret_cast<uint32_t*>(&h3);
+            // half of the math runs before the staging wait (register budget:
+            // four warps per SMSP leave 128 registers a thread)
+            if (j == 1) {
+              wait_staging();
+              *reinterpret_cast<uint4*>(stX + sw(lane, 0)) = dpk[0];
+              *reinterpret_cast<uint4*>(stX + sw(lane, 1)) = dpk[1];
+            } else if (j > 1) {
+              *reinterpret_cast<uint4*>(stX + sw(lane, j)) = dpk[j];
+            }
           }
         } else if (p.epi == kMul) {
 #pragma unroll
@@ -573,6 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             }
           }
         }
+        wait_staging();
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           uint4 pk;
