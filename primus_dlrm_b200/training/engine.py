@@ -194,15 +194,43 @@ class TrainEngine:
 
 
 def _make_shampoo(params, tc):
-    """Distributed Shampoo (optional dependency, ``dist_trainer.py:175-230``)."""
+    """Distributed Shampoo over the dense parameters (optional dependency
+    ``distributed_shampoo``; settings as ``primus_dlrm/training/dist_trainer.py:175-230``):
+    AdaGrad grafting, root-inverse preconditioner (bf16 factor matrices with an
+    eigendecomposition when ``shampoo_use_bf16_factor_matrix``), the DDP
+    distributed config when ``shampoo_use_ddp_distributed_config``, and the
+    momentum / Nesterov / decoupled-weight-decay switches where the installed
+    version accepts them."""
     try:
+        import inspect
+
         from distributed_shampoo import DistributedShampoo
-        from distributed_shampoo.shampoo_types import AdaGradPreconditionerConfig
+        from distributed_shampoo.shampoo_types import (AdaGradPreconditionerConfig, DDPDistributedConfig,
+                                                       RootInvShampooPreconditionerConfig)
     except ImportError as e:
         raise RuntimeError("dense_optimizer='shampoo' needs the distributed_shampoo package "
                            "(facebookresearch/optimizers), which is not installed") from e
-    return DistributedShampoo(params, lr=tc.lr, betas=(0.9, 1.0), epsilon=1e-4, weight_decay=tc.weight_decay,
-                              max_preconditioner_dim=tc.shampoo_max_preconditioner_dim,
-                              precondition_frequency=tc.shampoo_precondition_frequency,
-                              start_preconditioning_step=tc.shampoo_precondition_frequency,
-                              grafting_config=AdaGradPreconditionerConfig(epsilon=1.4285714285714e-05))
+    if tc.shampoo_use_bf16_factor_matrix:
+        from distributed_shampoo.preconditioner.matrix_functions_types import EigenConfig
+        precond = RootInvShampooPreconditionerConfig(amortized_computation_config=EigenConfig(),
+                                                     factor_matrix_dtype=torch.bfloat16,
+                                                     inverse_exponent_override={1: 0.5, 2: 0.5},
+                                                     num_tolerated_failed_amortized_computations=0)
+    else:
+        precond = RootInvShampooPreconditionerConfig()
+    kw = dict(lr=tc.lr, betas=(0.9, 1.0), epsilon=1e-4, weight_decay=tc.weight_decay,
+              max_preconditioner_dim=tc.shampoo_max_preconditioner_dim,
+              precondition_frequency=tc.shampoo_precondition_frequency,
+              start_preconditioning_step=tc.shampoo_precondition_frequency,
+              grafting_config=AdaGradPreconditionerConfig(epsilon=1.0 / 70000.0),
+              preconditioner_config=precond)
+    if tc.shampoo_use_ddp_distributed_config:
+        kw["distributed_config"] = DDPDistributedConfig(num_trainers_per_group=tc.shampoo_ddp_num_trainers_per_group,
+                                                        communicate_params=tc.shampoo_ddp_communicate_params)
+    accepted = inspect.signature(DistributedShampoo.__init__).parameters
+    for key, val in (("momentum", tc.shampoo_momentum), ("use_nesterov", tc.shampoo_use_nesterov),
+                     ("use_bias_correction", True),
+                     ("use_decoupled_weight_decay", tc.shampoo_use_decoupled_weight_decay)):
+        if key in accepted:
+            kw[key] = val
+    return DistributedShampoo(params, **kw)
