@@ -229,19 +229,23 @@ class A2AExecutor:
                 keep_all.append(keep)
             rows = torch.cat(rows)
             r_grads = self._a2a(rows[perm], send_l, recv_l)
+            # positions that contribute nothing (pooled pad ids) must not reach
+            # the optimizer at all: a zero gradient row would still take the
+            # weight-decay step of row-wise Adagrad / Adam
+            r_keep = self._a2a(torch.cat(keep_all)[perm].to(torch.uint8), send_l, recv_l).bool()
             dp_tables = []
             for ti in r_tab.unique().tolist():
                 t = spec.tables[ti]
                 if getattr(t, "kind", "local") == "data_parallel":
                     dp_tables.append(ti)
                     continue
-                m = r_tab == ti
+                m = (r_tab == ti) & r_keep
                 eager_sparse_update(t, spec.optimizer, r_keys[m], r_grads[m])
             # replicated tables: every rank applies everybody's rows
             all_dp = [ti for ti in sorted({spec.slots[i].table for i in sidx})
                       if getattr(spec.tables[ti], "kind", "local") == "data_parallel"]
             for ti in all_dp:
-                m = r_tab == ti
+                m = (r_tab == ti) & r_keep
                 k, gr = r_keys[m], r_grads[m]
                 n = torch.tensor([k.numel()], device=k.device)
                 ns = [torch.zeros_like(n) for _ in range(self.world)]
