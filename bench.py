@@ -5,7 +5,7 @@
     torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
 
 Per rank: batch 2048 (global 2048 x N, weak scaling), synthetic Zipf data of
-the BASELINE v6 shapes, random-init weights, bf16 compute, fp32 embedding
+the benchmark v6 shapes, random-init weights, bf16 compute, fp32 embedding
 tables row-wise sharded over the ranks, Adam sparse optimizer fused into the
 lookup backward, AdamW dense with clipping.
 

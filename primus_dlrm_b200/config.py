@@ -7,7 +7,7 @@ public contract shared with Primus-DLRM configs, so every reference YAML in
 Differences from the reference are additive only:
 
 * ``DataConfig.history_lengths`` -- per sequence-group history length
-  (BASELINE v6/5B configs use pools of 512/128/256).
+  (the v6 and ~5B benchmark configs use pools of 512/128/256).
 * ``SyntheticDataConfig`` -- Zipf id sampling, per-task Bernoulli rates,
   regression labels, dense-feature distributions, log-uniform table sizes.
 * ``TransformerConfig.norm`` -- ``rmsnorm`` (reference) or ``layernorm``.
@@ -47,7 +47,7 @@ class SchemaConfig:
 @dataclass
 class SyntheticDataConfig:
     """Synthetic data generator (``primus_dlrm/config.py:274-297``) plus the
-    BASELINE extensions (distribution knobs)."""
+    benchmark extensions (distribution knobs)."""
     enabled: bool = False
     seed: int = 42
     num_samples: int = 100_000

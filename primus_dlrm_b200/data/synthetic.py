@@ -4,7 +4,7 @@ Behaviour of the reference generator (``primus_dlrm/data/synthetic.py``):
 uniform ``randint`` ids, uniform dense features, one Bernoulli rate for every
 task, one history length, optional variable lengths (``<key>__lengths``).
 This module keeps that behaviour as the default and adds the distributions
-the BASELINE configs name:
+the benchmark configs name:
 
 * ``id_distribution: zipf`` -- Zipf(alpha) ranks drawn by inverse-CDF of the
   continuous power law, scattered over the id space by a bijective affine map

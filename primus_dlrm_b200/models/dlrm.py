@@ -6,7 +6,7 @@ sequence features + raw user dense -> bottom MLP; item tower = item scalars
 + projected dense + raw item dense -> bottom MLP; interaction over
 [user] x [item (+ ReLU-projected cross counters)]; one head per task.
 
-``dlrm_layout: criteo`` (BASELINE DLRM-DCNv2 config, additive): all dense
+``dlrm_layout: criteo`` (the DLRM-DCNv2 benchmark config, additive): all dense
 features -> bottom MLP; every scalar (single-id) sparse feature is one
 embedding; interaction over [bottom-MLP output] x [embeddings]; heads.
 """

@@ -5,7 +5,7 @@
   triangle) + the projected features, then the top MLP.
 * ``DCNv2``          -- cross layers ``x_{l+1} = x0 * (x_l W + b) + x_l`` with a
   deep MLP in parallel and a combining Linear.  ``low_rank > 0`` factors
-  ``W = U V^T`` (rank r), the form the BASELINE DLRM-DCNv2 config uses
+  ``W = U V^T`` (rank r), the form the DLRM-DCNv2 benchmark config uses
   (rank 512); ``low_rank = 0`` is the reference's full-rank cross.
 
 On CUDA in bf16 the MLPs and the low-rank cross layers run on the tcgen05

@@ -1,6 +1,6 @@
 #!/usr/bin/env python3
 """Embedding lookup + exchange micro-benchmark (the lookup / all-to-all sweep
-of the BASELINE micro-bench config): one table sharded over the ranks,
+of the embedding micro-benchmark config): one table sharded over the ranks,
 ``--ids`` ids per sample (sequence lookup) or pooled bags of ``--pooling``
 ids, Zipf-distributed ids. Forward (lookup + exchange into the consumer's
 activation buffer) and backward (gradient exchange + fused sparse optimizer)
