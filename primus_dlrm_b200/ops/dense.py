@@ -342,6 +342,13 @@ def linear(lin: nn.Linear, x: torch.Tensor, act: str | None = None) -> torch.Ten
     return y
 
 
+def _rows_strided_ok(t: torch.Tensor) -> bool:
+    """[B, L, N] bf16 view with contiguous rows and TMA-legal strides (a token
+    range of a wider [B, T, N] buffer)."""
+    return (t.dim() == 3 and t.stride(2) == 1 and t.stride(1) == t.shape[2] and (t.stride(0) * 2) % 16 == 0
+            and t.data_ptr() % 16 == 0 and t.shape[1] % 64 == 0)
+
+
 class _MLP2Native(torch.autograd.Function):
     """y = W2 GELU(W1 x + b1) + b2 (+ addend[l]) on the tcgen05 GEMM: the bias
     and GELU (with GELU' of the pre-activation stored for backward) fused into
@@ -378,21 +385,29 @@ class _MLP2Native(torch.autograd.Function):
     def backward(ctx, dout):
         xb, h, dact, w1b, w2b = ctx.saved_tensors
         dt_w1, dt_b1, dt_w2, dt_b2, has_add, dt_add = ctx.meta
-        dout = dout.contiguous().to(torch.bfloat16)
+        dout = dout.to(torch.bfloat16)
         B, L, N = dout.shape
         F_, K = w1b.shape
         rows = B * L
         v = lambda t: t.reshape(1, rows, t.shape[-1])  # noqa: E731
+        # a tokenizer's output gradient arrives as a strided view (its token
+        # range of the layer input's gradient): the GEMMs read it in place,
+        # one batch per sample, instead of copying it
+        strided = not dout.is_contiguous() and _rows_strided_ok(dout)
+        if not strided:
+            dout = dout.contiguous()
+        d3 = dout if strided else v(dout)
         dpre = torch.empty(B, L, F_, dtype=torch.bfloat16, device=dout.device)
-        tc_gemm(v(dout), w2b.reshape(1, N, F_), v(dpre), "mul", R=v(dact), b_kn=True)
+        tc_gemm(d3, w2b.reshape(1, N, F_), dpre if strided else v(dpre), "mul",
+                R=dact if strided else v(dact), b_kn=True)
         dx = torch.empty(B, L, K, dtype=torch.bfloat16, device=dout.device)
         tc_gemm(v(dpre), w1b.reshape(1, F_, K), v(dx), b_kn=True)
-        d2 = dout.reshape(rows, N)
         dp = dpre.reshape(rows, F_)
         if _wgrad_ok(dout, N, F_):
-            dw2 = tc_wgrad(v(dout), v(h), torch.zeros(1, N, F_, device=dout.device))[0].to(dt_w2)
+            dw2 = tc_wgrad(d3, h if strided else v(h), torch.zeros(1, N, F_, device=dout.device),
+                           l_sum=strided)[0].to(dt_w2)
         else:
-            dw2 = torch.mm(d2.t(), h.reshape(rows, F_), out_dtype=torch.float32).to(dt_w2)
+            dw2 = torch.mm(dout.reshape(rows, N).t(), h.reshape(rows, F_), out_dtype=torch.float32).to(dt_w2)
         if _wgrad_ok(dpre, F_, K):
             dw1 = tc_wgrad(v(dpre), v(xb), torch.zeros(1, F_, K, device=dout.device))[0].to(dt_w1)
         else:

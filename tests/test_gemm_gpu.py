@@ -232,3 +232,28 @@ def test_tokenizer_mlp_native_matches_torch():
     for got, exp in zip(grads, ref):
         err = (got.float() - exp).abs().max().item()
         assert err / (exp.abs().max().item() + 1e-6) < 3e-2
+
+
+def test_tokenizer_mlp_backward_reads_strided_gradient_in_place():
+    """The tokenizer MLP's backward with its output gradient as a token range
+    of a wider [B, T, N] buffer (what the concatenation of the S pools hands
+    it) against the same gradient made contiguous."""
+    from primus_dlrm_b200.ops import dense
+    torch.manual_seed(5)
+    Bsz, L, T, K, N = 96, 128, 320, 384, 256
+    l1 = torch.nn.Linear(K, N, device="cuda")
+    l2 = torch.nn.Linear(N, N, device="cuda")
+    pos = (torch.randn(L, N, device="cuda") * 0.1).requires_grad_(True)
+    x = (_bf(Bsz, L, K) * 0.5).requires_grad_(True)
+    G = _bf(Bsz, T, N)
+    grads = []
+    for strided in (True, False):
+        for t in (x, pos, l1.weight, l1.bias, l2.weight, l2.bias):
+            t.grad = None
+        y = dense.mlp2(x, l1, l2, addend=pos)
+        dout = G[:, 64:64 + L]
+        assert not dout.is_contiguous()
+        y.backward(dout if strided else dout.contiguous())
+        grads.append([t.grad.float().clone() for t in (x, pos, l1.weight, l1.bias, l2.weight, l2.bias)])
+    for name, a, b in zip(["x", "pos", "w1", "b1", "w2", "b2"], *grads):
+        torch.testing.assert_close(a, b, rtol=1e-2, atol=1e-2 * (b.abs().max().item() + 1e-3), msg=name)
