@@ -322,3 +322,40 @@ def test_fsdp_candidate_scoring_matches_unsharded():
         want = score_candidates(ref, user, cand, "listen_plus")
     for got in res.values():
         torch.testing.assert_close(got, want, rtol=1e-4, atol=1e-5)
+
+
+def _cli_worker(rank, world, tmp, dense, phase):
+    """scripts/run_distributed.py end to end on gloo ranks: phase 1 trains with
+    an epoch checkpoint and the ranking evaluation, phase 2 (fresh processes)
+    resumes from that checkpoint."""
+    import importlib.util
+
+    import torch.distributed as dist
+
+    from primus_dlrm_b200.config import Config
+    p = os.path.join(tmp, "cfg.yaml")
+    if phase == 1 and rank == 0:
+        cfg = Config.load(TINY)
+        cfg.data.history_length = 8
+        cfg.train.save_checkpoint = True
+        cfg.data.synthetic.num_prebatched = 2
+        cfg.save(p)
+    dist.barrier()
+    spec = importlib.util.spec_from_file_location("_rd", os.path.join(ROOT, "scripts", "run_distributed.py"))
+    rd = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(rd)
+    res = os.path.join(tmp, "results")
+    args = ["--config", p, "--results-dir", res, "--run-name", "r", "--kernels", "eager",
+            "--dense-strategy", dense, "--log-interval", "1"]
+    if phase == 1:
+        args += ["--max-steps", "3", "--eval-num-candidates", "32"]
+    else:
+        args += ["--max-steps", "5", "--resume", "latest", "--skip-eval"]
+    rd.main(args)          # ends by destroying the process group
+    return torch.load(os.path.join(res, "r", "checkpoints", "epoch_0.pt"), weights_only=False)["global_step"]
+
+
+@pytest.mark.parametrize("dense", ["fsdp", "zero2"])
+def test_run_distributed_cli_on_gloo_ranks(tmp_path, dense):
+    assert run_ranks(_cli_worker, 2, str(tmp_path), dense, 1, timeout=300)[0] == 3
+    assert run_ranks(_cli_worker, 2, str(tmp_path), dense, 2, timeout=300)[0] == 5
