@@ -38,7 +38,7 @@ sys.path.insert(0, ROOT)
 
 CONFIG = os.path.join(ROOT, "configs", "bench_onetrans_v6_b200.yaml")
 PER_GPU_BATCH = 2048
-METRIC = "train samples/sec (device-timed, max over ranks)"
+METRIC = "train samples/sec (box, device-timed, max over ranks) at 1/2/4/8 B200; exposed a2a ms/step"
 MODEL_DESC = "OneTrans v6-shaped: 8L d256 8hx32 NS16 pools 512/128/256 E128 Zipf1.05"
 
 
