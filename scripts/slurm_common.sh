@@ -11,7 +11,7 @@ slurm_usage() {
 usage: launch_slurm[_docker].sh --config <yaml> [options] [-- <extra run_distributed.py flags>]
   --nnodes N            nodes (default 1)            --gpus N           GPUs per node (default 8)
   --max-steps N         0 = the config's epochs      --run-name NAME    (default dist_slurm)
-  --results-dir DIR     (default results)            --dense-strategy   ddp | fsdp | dmp (default ddp)
+  --results-dir DIR     (default results)            --dense-strategy   ddp | fsdp | zero2 | dmp (default ddp)
   --data-root DIR       dataset root override        --log-interval N   (default 1000)
   --partition P         --time HH:MM:SS (12:00:00)   --job-name NAME    --account A
   --nodelist L          --dependency D               --reservation R    --qos Q
@@ -76,7 +76,7 @@ slurm_main() {
   [[ -n "$CONFIG" ]] || { echo "--config is required" >&2; slurm_usage; return 2; }
   [[ "$NNODES" =~ ^[1-9][0-9]*$ && "$GPUS" =~ ^[1-9][0-9]*$ ]] || { echo "--nnodes/--gpus must be positive integers" >&2; return 2; }
   [[ "$MAX_STEPS" =~ ^[0-9]+$ && "$RDZV_PORT" =~ ^[0-9]+$ ]] || { echo "--max-steps/--rdzv-port must be integers" >&2; return 2; }
-  case "$DENSE_STRATEGY" in ddp|fsdp|dmp) ;; *) echo "--dense-strategy must be ddp, fsdp or dmp" >&2; return 2 ;; esac
+  case "$DENSE_STRATEGY" in ddp|fsdp|zero2|dmp) ;; *) echo "--dense-strategy must be ddp, fsdp, zero2 or dmp" >&2; return 2 ;; esac
   case "$SUBMIT" in sbatch|srun) ;; *) echo "--submit must be sbatch or srun" >&2; return 2 ;; esac
   local cfg_abs="$CONFIG"
   [[ "$cfg_abs" == /* ]] || cfg_abs="$PROJECT/$CONFIG"

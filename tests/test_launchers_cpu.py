@@ -53,7 +53,7 @@ def test_dry_run_renders_valid_batch_script(script, tmp_path):
 
 @pytest.mark.parametrize("args,msg", [(["--config", "missing.yaml"], "config not found"),
                                       (["--nnodes", "0"], "positive integers"),
-                                      (["--dense-strategy", "zero"], "ddp, fsdp or dmp"),
+                                      (["--dense-strategy", "zero"], "ddp, fsdp, zero2 or dmp"),
                                       (["--bogus"], "unknown flag")])
 def test_bad_arguments_exit_2(args, msg):
     r = _render("launch_slurm.sh", *args)
