@@ -359,3 +359,19 @@ def _cli_worker(rank, world, tmp, dense, phase):
 def test_run_distributed_cli_on_gloo_ranks(tmp_path, dense):
     assert run_ranks(_cli_worker, 2, str(tmp_path), dense, 1, timeout=300)[0] == 3
     assert run_ranks(_cli_worker, 2, str(tmp_path), dense, 2, timeout=300)[0] == 5
+
+
+@pytest.mark.parametrize("dense,opt,tab_atol", [("ddp", "sgd", 1e-6), ("fsdp", "adam", 5e-4)])
+def test_sharded_training_matches_single_process_at_4_ranks(dense, opt, tab_atol):
+    """The same oracle comparison with 4 ranks: row-wise shards of 4, column
+    blocks of 4, a table owned by rank 1, FSDP shards of a quarter."""
+    world = 4
+    res = run_ranks(_dist_worker, world, dense, opt, 2)
+    ref_losses, ref_sd = _oracle(dense, opt, 2, world=world)
+    for r in range(world):
+        assert res[r][0] == pytest.approx(ref_losses, rel=1e-4, abs=1e-5)
+    sd = res[0][1]
+    assert set(sd) == set(ref_sd)
+    for k in ref_sd:
+        atol = tab_atol if ".embeddings." in k else 5e-5
+        torch.testing.assert_close(sd[k], ref_sd[k], rtol=1e-3, atol=atol, msg=lambda m: f"{k}: {m}")
