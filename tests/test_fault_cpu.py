@@ -146,12 +146,14 @@ def test_health_monitor_single_process_is_inert():
 
 @pytest.mark.parametrize("mode", ["raise", "exit"])
 def test_every_survivor_of_three_stops(mode):
-    """With three ranks, both survivors learn of rank 1's failure through the
-    store and stop before the same step."""
+    """With three ranks, both survivors stop before the same step and name
+    rank 1 as the origin: directly, or through the other survivor's report
+    when that one published first (its reason carries rank 1's)."""
     res, errs, codes = run_ranks_collect(_trainer_rank, 3, mode, timeout=120, pg_timeout=20)
     for r in (0, 2):
         assert r in res, errs.get(r)
-        assert res[r].get("peer_failure") == 1, res[r]
+        assert res[r].get("peer_failure") in (1, 2 - r), res[r]
+        assert res[r]["peer_failure"] == 1 or "rank 1" in res[r]["reason"], res[r]
         assert res[r]["step"] == 3, (res[r], errs)
     if mode == "exit":
         assert codes[1] == 3
