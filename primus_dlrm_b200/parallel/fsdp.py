@@ -213,14 +213,23 @@ class ShardedAdamW(torch.optim.Optimizer):
             return DTensor.from_local(t, p.device_mesh, p.placements, shape=p.shape, stride=p.stride())
         return t
 
-    def full_state_dict(self) -> dict:
-        """Unsharded moments (collective: every rank calls it; CPU tensors)."""
-        ea = [full_tensor(self._as_param(p, m)).cpu() for p, m in zip(self.plist, self.exp_avg)]
-        es = [full_tensor(self._as_param(p, v)).cpu() for p, v in zip(self.plist, self.exp_avg_sq)]
+    def full_state_dict(self, dst: int = 0) -> dict:
+        """Unsharded moments (collective: every rank calls it). Each moment is
+        gathered one parameter at a time on the device; only ``dst`` keeps the
+        CPU copies (other ranks get ``None`` entries), so no rank but ``dst``
+        holds the full optimizer state in host memory."""
+        keep = self.rank == dst
+
+        def gather(p, t):
+            full = full_tensor(self._as_param(p, t))
+            return full.cpu() if keep else None
+        ea = [gather(p, m) for p, m in zip(self.plist, self.exp_avg)]
+        es = [gather(p, v) for p, v in zip(self.plist, self.exp_avg_sq)]
         return {"step": self.step_count, "exp_avg": ea, "exp_avg_sq": es,
                 "param_groups": [{k: v for k, v in g.items() if k != "params"} for g in self.param_groups]}
 
-    state_dict = full_state_dict
+    def state_dict(self) -> dict:
+        return self.full_state_dict()
 
     def load_state_dict(self, sd) -> None:
         self.step_count = int(sd["step"])
